@@ -1,0 +1,318 @@
+"""Benchmark of the FlashDiffusion DMAP matvec on B200 (kernel evals/s = N_q * N_k / t).
+
+Workload (default, ``--config c2``): configuration 2 of the benchmark set —
+N = 200,000 points in d = 64 from a seeded 10-component Gaussian mixture,
+median-rule beta, alpha = 0.5, one N(0,1) right-hand side; bf16 tensor-core
+tiles, fp32 accumulation.  A step is one normalised DMAP matvec
+out = rscale * K(rscale * v) over all N x N pairs (row-sharded over the GPUs
+for N > 1, followed by the NCCL all-gather of the output shards).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+       (N > 1: launched by torch.distributed.run, one rank per GPU)
+
+The reference arm (--impl reference) times the reference algorithm's own CPU
+implementation (the NumPy tile loop, restated in oracle/fd_oracle.py and
+pinned to the reference's outputs) on the host cores, each step a bounded
+seeded row sample of the same workload, scaled to evals/s.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "c2": dict(workload="c2: DMAP matvec, Gaussian mixture N=200000 d=64, r=1, alpha=0.5", n=200_000, d=64),
+    "c5": dict(workload="c5: DMAP matvec, tanh manifold N=1000000 d=128, r=1, alpha=0.5", n=1_000_000, d=128),
+}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    p.add_argument("--no-lanczos", action="store_true")
+    p.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU sample (0 = auto)")
+    return p.parse_args()
+
+
+def make_data(cfg, seed=0):
+    from flashdiffusion_b200 import synthetic
+    if cfg == "c2":
+        X, beta = synthetic.gaussian_mixture(n=CONFIGS[cfg]["n"], d=CONFIGS[cfg]["d"], seed=seed)
+    else:
+        X, beta = synthetic.tanh_manifold(n=CONFIGS[cfg]["n"], d=CONFIGS[cfg]["d"], seed=seed)
+    return X, beta
+
+
+def cpu_sample(X, beta, rows, seed=0):
+    """Time the reference algorithm (NumPy tile loop) on `rows` seeded rows x all keys.
+
+    Returns (evals/s, seconds, rows).  The DMAP scales are set to ones for the
+    sample: they cost O(N) and do not change the tile loop being timed."""
+    from oracle import fd_oracle as O
+    idx = np.sort(np.random.default_rng(seed).choice(X.shape[0], rows, replace=False))
+    v = np.random.default_rng(seed + 1).standard_normal((X.shape[0], 1))
+    O.flash_diffusion(X[idx[:64]], X[:4096], v[:4096], beta)          # warm BLAS threads
+    t0 = time.perf_counter()
+    O.flash_diffusion(X[idx], X, v, beta)
+    dt = time.perf_counter() - t0
+    return rows * X.shape[0] / dt, dt, rows
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get("sm_max_mhz", 1965.0), "measured"
+    return 6650.0, 1590.0, 1965.0, "fallback"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    X, beta = make_data(args.config)
+    rows = args.cpu_rows or (256 if args.config == "c2" else 64)
+    cores = os.cpu_count()
+    for _ in range(args.warmup):
+        cpu_sample(X, beta, min(rows, 64))
+    vals = []
+    for s in range(args.steps):
+        ev, dt, _ = cpu_sample(X, beta, rows, seed=s)
+        vals.append(ev)
+    v = float(np.mean(vals))
+    n = cfg["n"]
+    line = {"impl": "reference", "metric": "kernel evals/sec per matvec (N^2/t)", "value": v, "unit": "evals/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * n * n / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 GEMM + f64 exp/accumulate", "data": "synthetic (seeded generator)",
+            "config": {"workload": cfg["workload"], "n": n, "d": cfg["d"], "sample_rows": rows,
+                       "parallelism": "host BLAS threads"},
+            "cpu_baseline": {"value": v, "unit": "evals/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows} seeded rows x all {n} keys per step, extrapolated to N^2"},
+            "e2e": {"value": v, "unit": "evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    from flashdiffusion_b200 import native
+    from flashdiffusion_b200.distributed import ShardedDMAP
+    native.require_device(local)
+    cfg = CONFIGS[args.config]
+    X, beta = make_data(args.config)
+    n, d = X.shape
+    dev = torch.device("cuda", local)
+    Xd = torch.from_numpy(X).to(dev)
+
+    # prepass (two Coifman-Lafon passes), timed once on the device
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    op = ShardedDMAP(Xd, beta, 0.5, "bf16")
+    setup_s = time.perf_counter() - t0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    op.fit()
+    e1.record()
+    torch.cuda.synchronize()
+    prepass_s = e0.elapsed_time(e1) / 1e3
+
+    v = torch.from_numpy(np.random.default_rng(1).standard_normal(n)).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)     # 256 MB > 126 MB L2
+
+    def step():
+        return op.matvec_device(v)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.25)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kst = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ken = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.zero_()                      # L2 flush between timed steps (outside the step events)
+        starts[i].record()
+        vl = op.matvec_local(v)
+        ken[i].record()
+        op.gather(vl)
+        ends[i].record()
+        kst[i] = starts[i]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    step_ms = float(np.sum([s.elapsed_time(e) for s, e in zip(starts, ends)])) / args.steps
+    kern_ms = float(np.sum([s.elapsed_time(e) for s, e in zip(kst, ken)])) / args.steps
+    t = torch.tensor([step_ms, kern_ms, prepass_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, kern_ms, prepass_s = [float(x) for x in t.cpu()]
+
+    # end to end through the public API with host buffers (N=1: DiffusionMap-style
+    # host matvec; N>1: each rank copies v in, runs its shard, gathers, copies out)
+    pinned_v = torch.from_numpy(np.random.default_rng(2).standard_normal(n)).pin_memory()
+    pinned_out = torch.empty(n, dtype=torch.float64).pin_memory()
+    for _ in range(2):
+        pinned_out.copy_(op.matvec_device(pinned_v.to(dev, non_blocking=True)))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(3, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        vd = pinned_v.to(dev, non_blocking=True)
+        pinned_out.copy_(op.matvec_device(vd), non_blocking=False)
+    torch.cuda.synchronize()
+    e2e_s = torch.tensor([(time.perf_counter() - t0) / e2e_steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_s.item())
+
+    # Lanczos time to k=16 eigenpairs (bf16 tiles, device fp64 basis), outside the timed region
+    lanczos = None
+    if not args.no_lanczos:
+        from flashdiffusion_b200.eigensolver import SolveInfo, trlan
+        info = SolveInfo()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        theta, _, res = trlan(op.matvec_device, n, 16, 1e-3, 200, 33, None, dev, info, stall_restarts=2)
+        torch.cuda.synchronize()
+        lt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(lt, op=dist.ReduceOp.MAX)
+        lanczos = {"k": 16, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tiles": "bf16",
+                   "max_rel_residual": float(np.max(res / np.abs(theta))), "top_eigenvalues": [float(x) for x in np.sort(theta)[::-1][:4]]}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    hbm, bf16_tf, sm_max, peak_src = load_peaks()
+    evals = float(n) * float(n)
+    value = evals / (step_ms / 1e3)
+    rows_local = op.rows[1] - op.rows[0]
+    kern_evals = float(rows_local) * n / (kern_ms / 1e3)
+    sm_clock = (clk or {}).get("sm_mhz") or sm_max
+    mufu_peak = 16 * 148 * sm_max * 1e6              # ex2 per s at max SM clock (nominal rate)
+    tensor_peak_evals = bf16_tf * 1e12 / (2 * d)
+    peak_evals = min(mufu_peak, tensor_peak_evals)
+    cpu_rows = args.cpu_rows or 256
+    cpu_ev, cpu_dt, _ = cpu_sample(X, beta, cpu_rows)
+    line = {
+        "metric": "kernel evals/sec per matvec (N^2/t)", "value": value, "unit": "evals/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded generator)",
+        "config": {"workload": cfg["workload"], "n": n, "d": d, "beta": beta, "tiles": "bf16 tcgen05",
+                   "parallelism": f"row-shard x{world}, NCCL all-gather", "l2": "flushed between steps (256 MB write)"},
+        "roofline": {"bound": "mufu", "achieved": kern_evals, "peak": peak_evals, "unit": "evals/s",
+                     "frac": kern_evals / peak_evals, "traffic": None,
+                     "mufu_peak": "16 ex2/clk/SM x 148 SMs x %.0f MHz (nominal rate, max clock)" % sm_max,
+                     "tensor": {"achieved": kern_evals * 2 * d / 1e12, "peak": bf16_tf, "unit": "TFLOP/s",
+                                "frac": kern_evals * 2 * d / 1e12 / bf16_tf, "peak_source": peak_src},
+                     "frac_at_sampled_clock": kern_evals / min(16 * 148 * sm_clock * 1e6, tensor_peak_evals)},
+        "cpu_baseline": {"value": cpu_ev, "unit": "evals/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{cpu_rows} seeded rows x all {n} keys (NumPy tile loop of the reference algorithm), {cpu_dt:.1f}s"},
+        "e2e": {"value": evals / e2e_s, "unit": "evals/s", "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n},
+        "gpu_launches": 3 * args.steps,
+        "prepass_s": prepass_s, "setup_s": setup_s, "kernel_ms": kern_ms,
+        "lanczos": lanczos, "clocks": clk,
+    }
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

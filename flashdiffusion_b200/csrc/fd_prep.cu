@@ -1,0 +1,238 @@
+// O(N) kernels around the O(N^2) tile kernels: norms, centring, operand
+// packing, right-hand-side preparation and Coifman-Lafon normalisation.
+// All of them are memory-bound one-pass kernels.
+#include "fd_prep.cuh"
+
+namespace fd {
+
+__global__ void sq_norms_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                                float* __restrict__ sq) {
+    // one warp per row, lanes stride the columns
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    float s = 0.f;
+    for (int k = lane; k < d; k += 32) {
+        const float v = (float)load_as_f64(X, dtype, row * d + k);
+        s = fmaf(v, v, s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) sq[row] = s;
+}
+
+// Column means of a strided subsample of at most `cap` rows (any shift is
+// exact for a translation-invariant kernel; the mean only minimises rounding).
+__global__ void mean_rows_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                                 int64_t stride, int64_t cnt, float* __restrict__ shift) {
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        double s = 0.0;
+        for (int64_t i = 0; i < cnt; ++i) s += load_as_f64(X, dtype, (i * stride) * d + c);
+        shift[c] = (float)(s / (double)cnt);
+    }
+}
+
+__device__ __forceinline__ void split3(double x, __nv_bfloat16& hi, __nv_bfloat16& mid,
+                                       __nv_bfloat16& lo) {
+    hi = __double2bfloat16(x);
+    const double r1 = x - (double)__bfloat162float(hi);
+    mid = __double2bfloat16(r1);
+    const double r2 = r1 - (double)__bfloat162float(mid);
+    lo = __double2bfloat16(r2);
+}
+
+// Packed bf16 operand (layout documented in fd_common.cuh).  One warp per row.
+__global__ void pack_bf16_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                                 const float* __restrict__ shift, double c2, int side, int kd,
+                                 __nv_bfloat16* __restrict__ out) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    __nv_bfloat16* o = out + row * kd;
+    const double scale = side == FD_SIDE_QUERY ? c2 : 1.0;
+    double ss = 0.0;
+    for (int k = lane; k < d; k += 32) {
+        double x = load_as_f64(X, dtype, row * d + k);
+        if (shift) x -= (double)shift[k];
+        const __nv_bfloat16 b = __double2bfloat16(x * scale);
+        const double bv = (double)__bfloat162float(b);
+        ss += bv * bv;
+        o[k] = b;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) {
+        // query: nq = -||q^||^2 / (2 c2); key: nk = -(c2/2) ||b||^2
+        const double nrm = side == FD_SIDE_QUERY ? -ss / (2.0 * c2) : -0.5 * c2 * ss;
+        __nv_bfloat16 h, m, l;
+        split3(nrm, h, m, l);
+        const __nv_bfloat16 one = __float2bfloat16(1.0f);
+        if (side == FD_SIDE_QUERY) {
+            o[d + 0] = one; o[d + 1] = one; o[d + 2] = one;
+            o[d + 3] = h; o[d + 4] = m; o[d + 5] = l;
+        } else {
+            o[d + 0] = h; o[d + 1] = m; o[d + 2] = l;
+            o[d + 3] = one; o[d + 4] = one; o[d + 5] = one;
+        }
+    }
+    for (int k = d + 6 + lane; k < kd; k += 32) o[k] = __float2bfloat16(0.0f);
+}
+
+// fp32 operand: centred points scaled by sqrt(beta) [n][dp], then n squared
+// norms of the stored values.  One warp per row.
+__global__ void pack_f32_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                                const float* __restrict__ shift, double sb, int dp,
+                                float* __restrict__ pts, float* __restrict__ sq) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    float s = 0.f;
+    for (int k = lane; k < dp; k += 32) {
+        float x = 0.f;
+        if (k < d) {
+            double xv = load_as_f64(X, dtype, row * d + k);
+            if (shift) xv -= (double)shift[k];
+            x = (float)(xv * sb);
+        }
+        pts[row * dp + k] = x;
+        s = fmaf(x, x, s);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) sq[row] = s;
+}
+
+// u[j*rc + c] = col_scale[j] * col_h[j] * V[j*ldv + c0 + c] for j < nk, 0 for nk <= j < nk_pad.
+__global__ void rhs_f32_kernel(const void* __restrict__ V, int v_dtype, int64_t nk, int64_t nk_pad,
+                               int ldv, int c0, int rc, const float* __restrict__ cs,
+                               const float* __restrict__ ch, float* __restrict__ u) {
+    const int64_t total = nk_pad * rc;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = e / rc;
+        const int c = (int)(e % rc);
+        float val = 0.f;
+        if (j < nk) {
+            double x = V ? load_as_f64(V, v_dtype, j * ldv + c0 + c) : 1.0;
+            if (cs) x *= (double)cs[j];
+            if (ch) x *= (double)ch[j];
+            val = (float)x;
+        }
+        u[e] = val;
+    }
+}
+
+// Transposed bf16 right-hand side for the P.V tensor-core product:
+// ut[c*ld + j] = bf16(col_scale[j] * col_h[j] * V[j*ldv + c0 + c]), zero beyond nk.
+__global__ void rhs_bf16t_kernel(const void* __restrict__ V, int v_dtype, int64_t nk, int64_t ld,
+                                 int ldv, int c0, int rc, const float* __restrict__ cs,
+                                 const float* __restrict__ ch, __nv_bfloat16* __restrict__ ut) {
+    const int64_t total = ld * rc;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = e / ld, j = e % ld;
+        float val = 0.f;
+        if (j < nk) {
+            double x = V ? load_as_f64(V, v_dtype, j * ldv + c0 + c) : 1.0;
+            if (cs) x *= (double)cs[j];
+            if (ch) x *= (double)ch[j];
+            val = (float)x;
+        }
+        ut[e] = __float2bfloat16(val);
+    }
+}
+
+__global__ void dmap_weights_kernel(const float* __restrict__ D, int64_t n, float alpha,
+                                    float* __restrict__ w) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        w[i] = (float)pow((double)D[i], -(double)alpha);
+}
+
+__global__ void dmap_rscale_kernel(const float* __restrict__ Kw, const float* __restrict__ w,
+                                   int64_t n, float* __restrict__ Da, float* __restrict__ rs) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const double da = (double)Kw[i] * (double)w[i];
+        if (Da) Da[i] = (float)da;
+        rs[i] = (float)(rsqrt(da) * (double)w[i]);
+    }
+}
+
+// ---- host launchers --------------------------------------------------------
+
+static int grid_for(int64_t n, int per_block) { return (int)cdiv(n, per_block); }
+
+int launch_sq_norms(const void* X, int dtype, int64_t n, int d, float* sq, cudaStream_t s) {
+    if (n == 0) return FD_OK;
+    sq_norms_kernel<<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, sq);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, cudaStream_t s) {
+    if (n == 0) {
+        FD_CUDA_TRY(cudaMemsetAsync(shift, 0, sizeof(float) * d, s));
+        return FD_OK;
+    }
+    const int64_t cap = 65536;
+    const int64_t stride = n > cap ? n / cap : 1;
+    const int64_t cnt = n > cap ? cap : n;
+    mean_rows_kernel<<<1, 256, 0, s>>>(X, dtype, n, d, stride, cnt, shift);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_pack(const void* X, int dtype, int64_t n, int d, const float* shift, float beta, int side,
+                int tile, void* op, cudaStream_t s) {
+    if (n == 0) return FD_OK;
+    if (tile == FD_TILE_BF16) {
+        const double c2 = 2.0 * (double)beta * 1.4426950408889634;  // 2 beta log2(e)
+        pack_bf16_kernel<<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, c2, side, kd_bf16(d),
+                                                       (__nv_bfloat16*)op);
+    } else {
+        const int dp = dp_f32(d);
+        float* pts = (float*)op;
+        float* sq = (float*)((char*)op + align256(sizeof(float) * (size_t)n * dp));
+        pack_f32_kernel<<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, sqrt((double)beta), dp,
+                                                      pts, sq);
+    }
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_rhs_f32(const void* V, int v_dtype, int64_t nk, int64_t nk_pad, int ldv, int c0, int rc,
+                   const float* cs, const float* ch, float* u, cudaStream_t s) {
+    const int64_t total = nk_pad * rc;
+    if (total == 0) return FD_OK;
+    const int grid = (int)std::min<int64_t>(cdiv(total, 256), 148 * 16);
+    rhs_f32_kernel<<<grid, 256, 0, s>>>(V, v_dtype, nk, nk_pad, ldv, c0, rc, cs, ch, u);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_rhs_bf16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0, int rc,
+                     const float* cs, const float* ch, __nv_bfloat16* ut, cudaStream_t s) {
+    const int64_t total = ld * rc;
+    if (total == 0) return FD_OK;
+    const int grid = (int)std::min<int64_t>(cdiv(total, 256), 148 * 16);
+    rhs_bf16t_kernel<<<grid, 256, 0, s>>>(V, v_dtype, nk, ld, ldv, c0, rc, cs, ch, ut);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_dmap_weights(const float* D, int64_t n, float alpha, float* w, cudaStream_t s) {
+    if (n == 0) return FD_OK;
+    dmap_weights_kernel<<<(int)std::min<int64_t>(cdiv(n, 256), 148 * 8), 256, 0, s>>>(D, n, alpha, w);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_dmap_rscale(const float* Kw, const float* w, int64_t n, float* Da, float* rs, cudaStream_t s) {
+    if (n == 0) return FD_OK;
+    dmap_rscale_kernel<<<(int)std::min<int64_t>(cdiv(n, 256), 148 * 8), 256, 0, s>>>(Kw, w, n, Da, rs);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+}  // namespace fd

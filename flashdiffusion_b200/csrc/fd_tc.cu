@@ -1,0 +1,395 @@
+// bf16 tensor-core path (FD_TILE_BF16) of the Gaussian-kernel operator on
+// sm_100a: a persistent, warp-specialised kernel.
+//
+//   out_i = ep_i * sum_j 2^( q~_i . k~_j ) * u_j          (q~.k~ <= 0 up to rounding)
+//
+// The packed operands fold the squared norms and -beta*log2(e) into the dot
+// product (layout in fd_common.cuh), so the whole exponent of one (i,j) pair
+// is a single tcgen05 MMA accumulator element; the epilogue is
+// clamp(<=0) -> MUFU ex2 -> FMA with u_j.
+//
+// CTA = 256 query rows (two 128-row subtiles sharing every key tile) x
+// stream of 128-row key tiles.  Warp roles (18 warps):
+//   warps 0-15  four epilogue warpgroups (subtile s, parity p): WG(s,p) owns the
+//               TMEM S buffer 2s+p and the key tiles of parity p of subtile s
+//   warp  16    TMA producer: query tile once per row tile, key tiles through
+//               a STAGES-deep shared-memory ring (no multicast)
+//   warp  17    MMA issuer: tcgen05.mma kind::f16, M=128 N=128 K=16 steps
+// Work split: the (row tile, key tile) pairs are cut into gridDim.x contiguous
+// ranges (persistent CTAs, one per SM).  A row tile fully inside one range is
+// written directly; a row tile cut between ranges leaves fp64 partials in the
+// workspace that tc_fixup_kernel sums in CTA order (deterministic).
+#include "fd_prep.cuh"
+#include "fd_ptx.cuh"
+
+namespace fd {
+
+__device__ int g_fd_status = 0;
+
+namespace tc {
+
+constexpr int BM = 128;     // rows per subtile = TMEM lanes
+constexpr int NSUB = 2;     // subtiles per CTA
+constexpr int ROWS = BM * NSUB;
+constexpr int BN = 128;     // key rows per tile = S columns
+constexpr int NEPI_WARPS = 16;
+constexpr int TMA_WARP = 16;
+constexpr int MMA_WARP = 17;
+constexpr int NTHREADS = 18 * 32;
+constexpr uint32_t BOX_BYTES = 128 * 128;  // one 128-row x 64-col bf16 box (128-byte rows)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per pipeline wait
+
+template <int KB>
+struct Cfg {
+    static constexpr int STAGES = KB == 1 ? 6 : (KB == 2 ? 4 : 2);
+    static constexpr uint32_t Q_BYTES = NSUB * KB * BOX_BYTES;
+    static constexpr uint32_t STAGE_BYTES = KB * BOX_BYTES;
+    static constexpr uint32_t BAR_OFF = Q_BYTES + STAGES * STAGE_BYTES;
+    // barriers: kfull[S], kempty[S], qfull, qempty, sfull[4], sempty[4], rfull[2], rempty[2], done
+    static constexpr int NBARS = 2 * STAGES + 2 + 8 + 4 + 1;
+    static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
+    static constexpr uint32_t RED_OFF = (MISC_OFF + 16 + 15) & ~15u;
+    static constexpr uint32_t SMEM_BYTES = RED_OFF + NSUB * BM * 8;
+    static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for 1024-byte alignment
+};
+
+struct Sched {
+    int64_t n_jt;    // key tiles per row tile
+    int64_t units;   // n_rt * n_jt
+    int grid;
+    __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }
+};
+
+__device__ __forceinline__ bool seg_end(int64_t n, int64_t n1, int64_t n_jt) {
+    return n + 1 == n1 || (n + 1) / n_jt != n / n_jt;
+}
+
+template <int KB>
+__global__ void __launch_bounds__(NTHREADS, 1)
+tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+          const float* __restrict__ u, int64_t nq, int kd, Sched sc, RowEpilogue ep,
+          double* __restrict__ part) {
+    using C = Cfg<KB>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = base;
+    uint8_t* sK = base + C::Q_BYTES;
+    uint64_t* bars = (uint64_t*)(base + C::BAR_OFF);
+    uint64_t* kfull = bars;
+    uint64_t* kempty = bars + C::STAGES;
+    uint64_t* qfull = bars + 2 * C::STAGES;
+    uint64_t* qempty = qfull + 1;
+    uint64_t* sfull = qfull + 2;
+    uint64_t* sempty = sfull + 4;
+    uint64_t* rfull = sempty + 4;
+    uint64_t* rempty = rfull + 2;
+    uint64_t* done = rempty + 2;
+    uint32_t* tmem_slot = (uint32_t*)(base + C::MISC_OFF);
+    volatile int* abort = (volatile int*)(base + C::MISC_OFF + 4);
+    double* red = (double*)(base + C::RED_OFF);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
+    const int64_t n_jt = sc.n_jt;
+    const int ksteps = kd / 16;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::STAGES; ++i) {
+            ptx::mbar_init(&kfull[i], 1);
+            ptx::mbar_init(&kempty[i], 1);
+        }
+        ptx::mbar_init(qfull, 1);
+        ptx::mbar_init(qempty, 1);
+        for (int i = 0; i < 4; ++i) {
+            ptx::mbar_init(&sfull[i], 1);
+            ptx::mbar_init(&sempty[i], 4);  // one arrive per epilogue warp
+        }
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&rfull[i], BM);
+            ptx::mbar_init(&rempty[i], BM);
+        }
+        ptx::mbar_init(done, 1);
+        *abort = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == MMA_WARP) {
+        ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    if (warp == TMA_WARP && lane == 0) {
+        ptx::prefetch_tmap(&tmq);
+        ptx::prefetch_tmap(&tmk);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == TMA_WARP) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t kph = 0, qcount = 0;
+            int64_t cur_rt = -1;
+            for (int64_t n = n0; n < n1; ++n) {
+                const int64_t rt = n / n_jt, jt = n - rt * n_jt;
+                if (rt != cur_rt) {
+                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                    ptx::mbar_expect_tx(qfull, C::Q_BYTES);
+                    for (int s = 0; s < NSUB; ++s)
+                        for (int kb = 0; kb < KB; ++kb)
+                            ptx::tma_load_2d(sQ + (s * KB + kb) * BOX_BYTES, &tmq, qfull, kb * 64,
+                                             (int)(rt * ROWS + s * BM));
+                    cur_rt = rt;
+                    ++qcount;
+                }
+                if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
+                for (int kb = 0; kb < KB; ++kb)
+                    ptx::tma_load_2d(sK + (stage * KB + kb) * BOX_BYTES, &tmk, &kfull[stage], kb * 64,
+                                     (int)(jt * BN));
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+        }
+    } else if (warp == MMA_WARP) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
+            const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
+            int stage = 0;
+            uint32_t kph = 0, qcount = 0;
+            int64_t cur_rt = -1;
+            for (int64_t n = n0; n < n1; ++n) {
+                const int64_t m = n - n0;
+                const int p = (int)(m & 1);
+                const uint32_t use = (uint32_t)(m >> 1);
+                const int64_t rt = n / n_jt;
+                if (rt != cur_rt) {
+                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                    ++qcount;
+                    cur_rt = rt;
+                }
+                if (!ptx::wait_bounded(&kfull[stage], kph, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                bool ok = true;
+                for (int s = 0; s < NSUB && ok; ++s) {
+                    const int b = s * 2 + p;
+                    if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    const uint32_t qa = q_base + s * KB * BOX_BYTES;
+                    const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                        ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(qa + off),
+                                     ptx::sw128_kmajor_desc(ka + off), idesc, ks > 0);
+                    }
+                    ptx::umma_commit(&sfull[b]);
+                }
+                if (!ok) break;
+                ptx::umma_commit(&kempty[stage]);
+                if (seg_end(n, n1, n_jt)) ptx::umma_commit(qempty);
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+            // every MMA issued above has completed once `done` flips
+            ptx::umma_commit(done);
+            ptx::wait_bounded(done, 0, abort, &g_fd_status, WAIT_LIMIT_NS);
+        }
+    } else {
+        // ---- epilogue warpgroups ------------------------------------------
+        const int wg = warp >> 2;
+        const int s = wg >> 1, p = wg & 1;
+        const int quarter = warp & 3;
+        const int row_in_tile = s * BM + quarter * 32 + lane;
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        const int64_t first_rt = n0 / n_jt;
+        double acc = 0.0;
+        uint32_t segs = 0;
+        bool alive = true;
+        for (int64_t n = n0; n < n1 && alive; ++n) {
+            const int64_t m = n - n0;
+            const int64_t rt = n / n_jt, jt = n - rt * n_jt;
+            if ((int)(m & 1) == p) {
+                const uint32_t use = (uint32_t)(m >> 1);
+                const int b = s * 2 + p;
+                if (!ptx::wait_bounded(&sfull[b], use & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ptx::tc_fence_after();
+                const float4* u4 = (const float4*)(u + jt * BN);
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 1
+                for (int ch = 0; ch < BN / 32; ++ch) {
+                    uint32_t v[32];
+                    ptx::tmem_ld32(t_lane + b * BN + ch * 32, v);
+                    ptx::tmem_wait_ld(v);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const float4 uu = __ldg(u4 + ch * 8 + g);
+                        a0 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 0]), 0.f)), uu.x, a0);
+                        a1 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 1]), 0.f)), uu.y, a1);
+                        a2 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 2]), 0.f)), uu.z, a2);
+                        a3 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 3]), 0.f)), uu.w, a3);
+                    }
+                }
+                acc += (double)((a0 + a1) + (a2 + a3));
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&sempty[b]);
+            }
+            if (seg_end(n, n1, n_jt)) {
+                // combine the two parity halves of this subtile, then store
+                const uint32_t ph = segs & 1;
+                if (p == 1) {
+                    if (!ptx::wait_bounded(&rempty[s], ph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    red[s * BM + quarter * 32 + lane] = acc;
+                    ptx::mbar_arrive(&rfull[s]);
+                } else {
+                    if (!ptx::wait_bounded(&rfull[s], ph, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    const double tot = acc + red[s * BM + quarter * 32 + lane];
+                    ptx::mbar_arrive(&rempty[s]);
+                    const int64_t gi = rt * ROWS + row_in_tile;
+                    const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
+                    const bool full = seg_first == 0 && jt == n_jt - 1;
+                    if (gi < nq) {
+                        if (full) store_out(ep, gi, 0, tot);
+                        else part[((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * ROWS + row_in_tile] = tot;
+                    }
+                }
+                acc = 0.0;
+                ++segs;
+            }
+        }
+        ptx::tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == MMA_WARP) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Sum the partials of row tiles cut between CTA ranges, in CTA order.
+__global__ void tc_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, RowEpilogue ep) {
+    const int64_t rt = blockIdx.x;
+    const int64_t lo = rt * sc.n_jt, hi = lo + sc.n_jt - 1;
+    auto owner = [&](int64_t n) {
+        int c = (int)(n * sc.grid / sc.units);
+        if (c >= sc.grid) c = sc.grid - 1;
+        while (c + 1 < sc.grid && sc.start(c + 1) <= n) ++c;
+        while (c > 0 && sc.start(c) > n) --c;
+        return c;
+    };
+    const int c_lo = owner(lo), c_hi = owner(hi);
+    if (c_lo == c_hi) return;
+    for (int r = threadIdx.x; r < ROWS; r += blockDim.x) {
+        const int64_t gi = rt * ROWS + r;
+        if (gi >= nq) continue;
+        double sum = 0.0;
+        for (int c = c_lo; c <= c_hi; ++c) {
+            const int64_t st = sc.start(c);
+            if (st == sc.start(c + 1)) continue;  // empty range
+            const int slot = (st / sc.n_jt == rt) ? 0 : 1;
+            sum += part[((int64_t)c * 2 + slot) * ROWS + r];
+        }
+        store_out(ep, gi, 0, sum);
+    }
+}
+
+}  // namespace tc
+
+// ---- host side -----------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static int get_encode(EncodeTiledFn* fn) {
+    static EncodeTiledFn cached = nullptr;
+    if (!cached) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        FD_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p)
+            return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
+        cached = (EncodeTiledFn)p;
+    }
+    *fn = cached;
+    return FD_OK;
+}
+
+// 2-D bf16 map over a [rows][cols] row-major matrix, 64 x box_rows boxes, 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+    EncodeTiledFn enc;
+    FD_TRY(get_encode(&enc));
+    FD_CHECK_ARG(((uintptr_t)ptr & 15) == 0, "tile operand must be 16-byte aligned");
+    FD_CHECK_ARG((cols * 2) % 16 == 0, "tile operand row pitch must be a multiple of 16 bytes");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return FD_OK;
+}
+
+static int num_sms() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
+    (void)nq; (void)nk; (void)rc;
+    return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS);
+}
+
+template <int KB>
+static int launch_tc_kb(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
+                        const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
+    using C = tc::Cfg<KB>;
+    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)C::SMEM_ALLOC));
+    tc::tc_kernel<KB><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, sc, ep, part);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_tc(const __nv_bfloat16* qop, int64_t nq, const __nv_bfloat16* kop, int64_t nk, int d,
+              const void* rhs, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (nq == 0) return FD_OK;
+    if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
+    if (rc != 1) return set_error(FD_ERR_UNSUPPORTED, "bf16 tile path: block right-hand sides not built yet");
+    const int kd = kd_bf16(d);
+    const int kb = (int)cdiv(kd, 64);
+    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "bf16 tile path supports d <= 186 (got d=%d)", d);
+    const size_t need = tc_workspace_bytes(nq, nk, rc);
+    if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "bf16 tile path: workspace %zu B < %zu B", ws_bytes, need);
+    CUtensorMap mq, mk;
+    FD_TRY(make_map(&mq, qop, nq, kd, tc::BM));
+    FD_TRY(make_map(&mk, kop, nk, kd, tc::BN));
+    tc::Sched sc;
+    sc.n_jt = cdiv(nk, tc::BN);
+    sc.units = cdiv(nq, tc::ROWS) * sc.n_jt;
+    sc.grid = (int)std::min<int64_t>(num_sms(), sc.units);
+    double* part = (double*)ws;
+    const float* u = (const float*)rhs;
+    switch (kb) {
+        case 1: FD_TRY(launch_tc_kb<1>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
+        case 2: FD_TRY(launch_tc_kb<2>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
+        default: FD_TRY(launch_tc_kb<3>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
+    }
+    tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(part, sc, nq, ep);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int read_and_clear_status(cudaStream_t s, int* status) {
+    int zero = 0;
+    FD_CUDA_TRY(cudaMemcpyFromSymbolAsync(status, g_fd_status, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+    FD_CUDA_TRY(cudaMemcpyToSymbolAsync(g_fd_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+    FD_CUDA_TRY(cudaStreamSynchronize(s));
+    return FD_OK;
+}
+
+}  // namespace fd

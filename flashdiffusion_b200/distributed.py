@@ -1,0 +1,115 @@
+"""Row-sharded operator over several GPUs of one node (one process per GPU).
+
+Sharding (the reference has no distributed code; this is new): output rows
+are independent given all of K and the full right-hand side, so rank r owns a
+contiguous block of 256-row tiles of Q and holds all of K.  A matvec is one
+local tile pass over the rank's rows followed by ONE collective, an NCCL
+all-gather of the output shards (NVLink / NVSwitch), so every rank ends with
+the full vector and can run the (replicated, deterministic) fp64 Krylov
+update locally.  The prepass needs the same gather twice (D, then K w).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+ROW_TILE = 256
+
+
+def shard_rows(n: int, world: int, rank: int, tile: int = ROW_TILE):
+    """[begin, end) rows of rank ``rank``: contiguous tiles, sizes differ by at most one tile."""
+    n_t = (n + tile - 1) // tile
+    t0 = rank * n_t // world
+    t1 = (rank + 1) * n_t // world
+    return min(t0 * tile, n), min(t1 * tile, n)
+
+
+def all_shards(n: int, world: int, tile: int = ROW_TILE):
+    return [shard_rows(n, world, r, tile) for r in range(world)]
+
+
+class RowGather:
+    """All-gather of uneven contiguous row shards into the full (n, r) array.
+
+    NCCL gathers equal-sized buffers, so shards are padded to the largest
+    shard and the valid rows are copied out afterwards (a device copy of n*r
+    elements).
+    """
+
+    def __init__(self, n: int, world: int, group=None):
+        self.n = n
+        self.world = world
+        self.group = group
+        self.shards = all_shards(n, world)
+        self.maxrows = max(b - a for a, b in self.shards)
+
+    def __call__(self, local: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return local
+        r = 1 if local.dim() == 1 else local.shape[1]
+        loc2 = local.reshape(local.shape[0], r)
+        pad = torch.zeros((self.maxrows, r), dtype=local.dtype, device=local.device)
+        pad[: loc2.shape[0]] = loc2
+        buf = torch.empty((self.world * self.maxrows, r), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(buf, pad, group=self.group)
+        out = torch.cat([buf[i * self.maxrows: i * self.maxrows + (b - a)] for i, (a, b) in enumerate(self.shards)])
+        return out.reshape(self.n) if local.dim() == 1 else out
+
+
+class ShardedDMAP:
+    """DMAP operator M = diag(rscale) K diag(rscale) row-sharded over the process group.
+
+    ``local_apply(V, col_scale, row_scale)`` is the rank's tile pass
+    (``GaussianOperator.apply`` on its rows by default); it can be replaced by
+    a host fake in tests.
+    """
+
+    def __init__(self, X: torch.Tensor, beta: float, alpha: float, precision: str = "bf16", group=None,
+                 local_apply: Optional[Callable] = None):
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n = X.shape[0]
+        self.rows = shard_rows(self.n, self.world, self.rank)
+        self.gather = RowGather(self.n, self.world, group)
+        if local_apply is None:
+            from . import native
+            from .kernel import GaussianOperator
+            shift = native.mean_rows(X)
+            a, b = self.rows
+            self.op = GaussianOperator(X[a:b], X, beta, precision, shift=shift)
+            self._apply = lambda V, cs, rs, dt: self.op.apply(V, col_scale=cs, row_scale=rs, out_dtype=dt)
+            self._weights = native.dmap_weights
+            self._rscale = native.dmap_rscale
+        else:
+            self._apply = local_apply
+            self._weights = lambda D, a_: D.double().pow(-a_).to(D.dtype)
+            self._rscale = lambda Kw, w: ((Kw.double() * w.double()).to(Kw.dtype),
+                                          ((Kw.double() * w.double()).rsqrt() * w.double()).to(Kw.dtype))
+        self.alpha = alpha
+        self.D = self.D_alpha = self.rscale = None
+        self.rscale_local = None
+
+    def fit(self):
+        """Two prepasses with a gather each: D = K 1, D_alpha = (K w) w, rscale."""
+        Dl = self._apply(None, None, None, torch.float32)[:, 0].contiguous()
+        D = self.gather(Dl).contiguous()
+        w = self._weights(D, self.alpha)
+        Kwl = self._apply(w, None, None, torch.float32)[:, 0].contiguous()
+        Kw = self.gather(Kwl).contiguous()
+        self.D = D
+        self.D_alpha, self.rscale = self._rscale(Kw, w)
+        a, b = self.rows
+        self.rscale_local = self.rscale[a:b].contiguous()
+        return self
+
+    def matvec_local(self, v: torch.Tensor, out_dtype=torch.float64) -> torch.Tensor:
+        squeeze = v.dim() == 1
+        out = self._apply(v[:, None] if squeeze else v, self.rscale, self.rscale_local, out_dtype)
+        return out[:, 0] if squeeze else out
+
+    def matvec_device(self, v: torch.Tensor) -> torch.Tensor:
+        """Full M v on every rank: local rows + one all-gather."""
+        return self.gather(self.matvec_local(v))

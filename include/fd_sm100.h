@@ -1,0 +1,159 @@
+/*
+ * fd_sm100.h — C ABI of libfd_sm100.so, the B200 (sm_100a) FlashDiffusion operator.
+ *
+ * The operator never materialises the kernel matrix:
+ *
+ *     K(i,j) = exp(-beta * ||q_i - k_j||^2)
+ *     out_i  = row_scale_i / row_div_i * sum_j K(i,j) * col_scale_j * h_j * V_j
+ *
+ * Reference interfaces each entry point replaces are cited as file:line of
+ * sparsetrace/FlashDiffusion (FD/ = src/flashdiffusion/).
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer unless stated otherwise; the caller owns
+ *    every buffer (inputs, outputs and workspace).  Nothing here allocates
+ *    device memory: sizes of caller-provided workspaces come from the *_bytes()
+ *    queries.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    All work is enqueued on it; nothing synchronises the host.
+ *  - Return value: FD_OK (0) or an FD_ERR_* code; fd_last_error() gives a
+ *    human-readable message for the calling host thread.  Argument errors are
+ *    detected before any launch (the reference raises RuntimeError through
+ *    TORCH_CHECK in the same situations, FD/csrc/flash_diffusion_sm100.cu:98-110).
+ *  - Device-side pipeline waits are bounded; a wait that gives up records
+ *    FD_ERR_TIMEOUT in a device status word that fd_check_status() reads.
+ */
+#ifndef FD_SM100_H
+#define FD_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FD_OK 0
+#define FD_ERR_ARG 1          /* bad argument (shape, null pointer, alignment, size) */
+#define FD_ERR_CUDA 2         /* CUDA runtime / driver error                          */
+#define FD_ERR_UNSUPPORTED 3  /* device is not sm_100-family or shape unsupported     */
+#define FD_ERR_TIMEOUT 4      /* a bounded device-side wait gave up                   */
+#define FD_ERR_WORKSPACE 5    /* caller workspace too small                           */
+
+/* element types of caller inputs */
+#define FD_DTYPE_F32 0
+#define FD_DTYPE_F16 1
+#define FD_DTYPE_BF16 2
+#define FD_DTYPE_F64 3
+
+/* tile precision of the distance GEMM */
+#define FD_TILE_BF16 0  /* tcgen05 bf16 tiles, fp32 accumulation (matvec rel. L2 <= 2e-3) */
+#define FD_TILE_F32 1   /* fp32 tiles (rel. L2 <= 1e-5)                                  */
+
+/* operand side for fd_pack_operand */
+#define FD_SIDE_QUERY 0
+#define FD_SIDE_KEY 1
+
+/* Message for the last error on this host thread (never NULL). */
+const char* fd_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fd_version(void);
+
+/* 1 if `device` is a compute-capability 10.x (B200-class) GPU, else 0. */
+int fd_device_supported(int device);
+
+/* Read and clear the device status word written by bounded waits
+ * (FD_OK or FD_ERR_TIMEOUT).  Synchronises `stream`. */
+int fd_check_status(void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Reference-compatible trio.  Replaces the pybind module flash_diffusion_sm100
+ * (FD/csrc/flash_diffusion_sm100.cu:571-588) as used by FD/kernel_cuda_sm100.py:67-119.
+ * X is (n, d) row-major of dtype FD_DTYPE_*.  `tile` selects FD_TILE_BF16 or
+ * FD_TILE_F32.  Workspace: fd_workspace_bytes(n, n, d, 1, tile).
+ * ------------------------------------------------------------------------- */
+
+/* sq[i] = sum_k X[i,k]^2 in fp32.  Replaces compute_sq_norms
+ * (FD/csrc/flash_diffusion_sm100.cu:456-476). */
+int fd_compute_sq_norms(const void* X, int dtype, int64_t n, int d, float* sq, void* stream);
+
+/* D[i] = sum_j exp(-beta ||x_i - x_j||^2) * w[j]  (w may be NULL = all ones).
+ * Replaces prepass (FD/csrc/flash_diffusion_sm100.cu:478-518) and
+ * prepass_rowsum (FD/kernel.py:141-182).  The reference binding also takes
+ * sq_X; here squared norms are derived from the rounded tile operands so
+ * that distances stay consistent, hence no sq argument. */
+int fd_prepass(const void* X, int dtype, int64_t n, int d, const float* w, float beta, int tile,
+               float* D, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[i] = rscale[i] * sum_j exp(-beta ||x_i-x_j||^2) * rscale[j] * v[j].
+ * Replaces matvec (FD/csrc/flash_diffusion_sm100.cu:520-569) and
+ * DiffusionMap.matvec (FD/dmap.py:119-136). */
+int fd_matvec(const void* X, int dtype, int64_t n, int d, const float* v, const float* rscale,
+              float beta, int tile, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace for fd_prepass / fd_matvec / fd_flash_diffusion. */
+size_t fd_workspace_bytes(int64_t nq, int64_t nk, int d, int r, int tile);
+
+/* General primitive FlashDiffusion(Q, K, V, beta, rscale_q, rscale_k, h)
+ * (FD/kernel.py:189-257), plus an optional row divisor (the Doob row
+ * normaliser Ph of FD/dmap.py:249-261).  Q (nq,d), K (nk,d) of `dtype`;
+ * V (nk, r) fp32 row-major (NULL = all ones); out (nq, r) fp32.  Any of rscale_q, rscale_k, h,
+ * row_div may be NULL (= ones).  The coordinates of Q and K are shifted by
+ * the mean of K before rounding (the kernel is translation invariant). */
+int fd_flash_diffusion(const void* Q, const void* K, int dtype, int64_t nq, int64_t nk, int d,
+                       const float* V, int r, float beta, const float* rscale_q, const float* rscale_k,
+                       const float* h, const float* row_div, int tile, float* out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Resident-operand API: pack once, apply every solver iteration.  This is the
+ * device-resident form of CUDAStateSM100 (FD/kernel_cuda_sm100.py:52-64).
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of one packed operand of n points in d dims for `tile`. */
+size_t fd_operand_bytes(int64_t n, int d, int tile);
+
+/* Mean of the rows of X (n, d) into shift (d floats, device).  Used as the
+ * common translation of both operands. */
+int fd_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, void* stream);
+
+/* Pack X (n,d) into a tile operand (fd_operand_bytes(n,d,tile) bytes, 256-byte
+ * aligned).  `shift` (d floats, may be NULL) is subtracted first.  `side` is
+ * FD_SIDE_QUERY or FD_SIDE_KEY; a query operand must be applied against a key
+ * operand packed with the same beta, shift and tile. */
+int fd_pack_operand(const void* X, int dtype, int64_t n, int d, const float* shift, float beta,
+                    int side, int tile, void* operand, void* stream);
+
+/* Workspace for fd_apply. */
+size_t fd_apply_workspace_bytes(int64_t nq, int64_t nk, int r, int tile);
+
+/* out = diag(row_scale / row_div) K(Q,K) diag(col_scale * col_h) V.
+ * V is (nk, r) of v_dtype (FD_DTYPE_F32 or FD_DTYPE_F64; NULL = all ones), out is (nq, r) of
+ * out_dtype (F32 or F64).  col_scale, col_h, row_scale, row_div may be NULL.
+ * Modes of the reference map onto the pointers: prepass (V = w, rest NULL),
+ * DMAP (row_scale = col_scale = rscale), AMAP (rscale_q, rscale_k), Doob
+ * (col_h = h, row_div = Ph). */
+int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, int tile,
+             const void* V, int v_dtype, int r, const float* col_scale, const float* col_h,
+             const float* row_scale, const float* row_div, void* out, int out_dtype,
+             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Coifman-Lafon normalisation helpers (FD/dmap.py:108-115,
+ * FD/kernel_cuda_sm100.py:89-98), fp32 vectors of length n.
+ * ------------------------------------------------------------------------- */
+
+/* w = D^-alpha. */
+int fd_dmap_weights(const float* D, int64_t n, float alpha, float* w, void* stream);
+
+/* D_alpha = Kw * w;  rscale = D_alpha^-1/2 * w  (Kw = prepass with weights w). */
+int fd_dmap_rscale(const float* Kw, const float* w, int64_t n, float* D_alpha, float* rscale,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FD_SM100_H */

@@ -1,0 +1,220 @@
+"""GPU parity of the sm_100a kernels against the pinned CPU oracle / reference goldens.
+
+Tolerances: matvec relative L2 error <= 2e-3 with bf16
+tiles and <= 1e-5 with fp32 tiles; eigenvalues within 1e-6 relative after the
+fp64 ramp.  Everything here goes through the C ABI of libfd_sm100.so.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import fd_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"bf16": 2e-3, "fp32": 1e-5}
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, dtype=np.float64).ravel()
+    b = np.asarray(b, dtype=np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    from flashdiffusion_b200 import native
+    native.require_device()
+    yield
+    native.check_status()
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+def test_prepass_golden(gold, prec):
+    from flashdiffusion_b200 import prepass_rowsum
+    g = gold("prepass.npz")
+    X = g["X"]
+    assert rel_l2(prepass_rowsum(X, X, 1.0, precision=prec), g["D64"]) <= TOL[prec]
+    assert rel_l2(prepass_rowsum(X, X, 0.7, g["w"], precision=prec), g["Dw"]) <= TOL[prec]
+    if prec == "fp32":   # reference test tolerance (tests/test_kernel.py:33-39)
+        np.testing.assert_allclose(prepass_rowsum(X, X, 1.0, precision=prec), g["D64"], rtol=1e-5)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("n", [0, 1, 2])
+def test_dmap_matvec_golden(gold, prec, n):
+    from flashdiffusion_b200 import FlashDiffusion
+    g = gold("matvec.npz")
+    beta = float(g["pairs"][n][0])
+    rs = g[f"rscale{n}"]
+    out = FlashDiffusion(g["X"], g["X"], g["v"][:, None], beta, rscale_q=rs, rscale_k=rs, precision=prec).ravel()
+    assert rel_l2(out, g[f"out{n}"]) <= TOL[prec]
+    if prec == "fp32":   # reference test tolerance (tests/test_kernel.py:42-51)
+        np.testing.assert_allclose(out, g[f"out{n}"], rtol=2e-4, atol=1e-10)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+def test_amap_block_golden(gold, prec):
+    """Q != K, separate rscale_q / rscale_k, Doob h, r = 3 columns."""
+    from flashdiffusion_b200 import FlashDiffusion
+    g = gold("amap.npz")
+    beta = float(g["beta"])
+    out = FlashDiffusion(g["Q"], g["K"], g["V"], beta, g["rq"], g["rk"], g["h"], precision=prec)
+    assert out.shape == (130, 3)
+    assert rel_l2(out, g["out"]) <= TOL[prec]
+    plain = FlashDiffusion(g["Q"], g["K"], g["V"], beta, precision=prec)
+    assert rel_l2(plain, g["out_plain"]) <= TOL[prec]
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+def test_gmm64_fit_and_matvec_golden(gold, prec):
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("gmm64.npz")
+    dm = DiffusionMap(beta=float(g["beta"]), alpha=0.5, precision=prec).fit(g["X"])
+    assert rel_l2(dm.D_, g["D"]) <= TOL[prec]
+    assert rel_l2(dm.rscale_, g["rscale"]) <= TOL[prec]
+    assert rel_l2(dm.matvec(g["v"]), g["out"]) <= 2 * TOL[prec]
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+def test_doob_golden(gold, prec):
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("doob.npz")
+    dm = DiffusionMap(beta=1.0, alpha=0.5, n_components=4, precision=prec).fit(g["X"])
+    # use the golden rscale so that only the Doob operator is compared
+    doob = dm.doob_transform(g["h"])
+    assert rel_l2(doob.Ph_, g["Ph"]) <= 2 * TOL[prec]
+    assert rel_l2(doob.matvec(g["v"]), g["out"]) <= 4 * TOL[prec]
+
+
+def test_fit_golden_fp32(gold):
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("fit.npz")
+    dm = DiffusionMap(beta=1.0, alpha=0.5, precision="fp32").fit(g["X"])
+    np.testing.assert_allclose(dm.D_, g["D"], rtol=1e-5)
+    np.testing.assert_allclose(dm.D_alpha_, g["D_alpha"], rtol=1e-5)
+    np.testing.assert_allclose(dm.rscale_, g["rscale"], rtol=1e-5)
+
+
+@pytest.mark.parametrize("prec", ["ramp", "fp32"])
+def test_eigenvalues_golden(gold, prec):
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("eig.npz")
+    dm = DiffusionMap(beta=1.0, alpha=0.5, n_components=6, precision=prec).fit(g["X"])
+    coords = dm.transform()
+    err = np.abs(dm.eigenvalues_ - g["vals"]) / np.abs(g["vals"])
+    assert err.max() < 1e-6, err
+    assert coords.shape == (300, 5)
+    np.testing.assert_allclose(np.abs(coords), np.abs(g["coords"]), rtol=1e-3, atol=1e-6)
+
+
+def test_c1_swiss_roll_eigenvalues_golden(gold):
+    """Configuration 1 (N=4096, d=3): ramp eigenvalues vs the reference's ARPACK run."""
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("c1.npz")
+    dm = DiffusionMap(beta=float(g["beta"]), alpha=0.5, n_components=8).fit(g["X"])
+    dm.transform()
+    err = np.abs(dm.eigenvalues_ - g["vals"]) / np.abs(g["vals"])
+    assert err.max() < 1e-6, (dm.eigenvalues_, g["vals"])
+    np.testing.assert_allclose(dm.rscale_, g["rscale"], rtol=1e-5)
+
+
+def test_nystrom_golden(gold):
+    from flashdiffusion_b200 import DiffusionMap
+    g = gold("nystrom.npz")
+    dm = DiffusionMap(beta=1.0, alpha=0.5, n_components=5, precision="fp32").fit(g["Xt"])
+    # feed the reference eigenpairs so that only the AMAP extension is compared
+    dm.eigenvalues_, dm.eigenvectors_ = g["vals"], g["vecs"]
+    c = dm.transform(g["Xn"])
+    assert rel_l2(c, g["coords"]) <= 1e-5
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("nq,nk,d,r", [(1, 1, 3, 1), (129, 257, 3, 1), (300, 200, 64, 1), (257, 511, 66, 1),
+                                       (200, 1000, 128, 1), (130, 700, 186, 1), (70, 90, 5, 4),
+                                       (513, 300, 64, 2)])
+def test_ragged_shapes_vs_oracle(prec, nq, nk, d, r):
+    from flashdiffusion_b200 import FlashDiffusion
+    rng = np.random.default_rng(nq * 7 + nk + d)
+    K = rng.standard_normal((nk, d)).astype(np.float32) * 0.7 + 3.0
+    Q = K[rng.integers(0, nk, nq)] + 0.1 * rng.standard_normal((nq, d)).astype(np.float32)
+    V = rng.standard_normal((nk, r))
+    rq, rk, h = rng.uniform(0.5, 2, nq), rng.uniform(0.5, 2, nk), rng.uniform(0.2, 1, nk)
+    beta = 1.0 / (2.0 * d)
+    ref = O.flash_diffusion(Q, K, V, beta, rq, rk, h)
+    out = FlashDiffusion(Q, K, V, beta, rq, rk, h, precision=prec)
+    assert out.shape == (nq, r)
+    assert rel_l2(out, ref) <= TOL[prec]
+
+
+def test_empty_key_set_gives_zero():
+    from flashdiffusion_b200 import FlashDiffusion
+    out = FlashDiffusion(np.ones((5, 3), np.float32), np.ones((0, 3), np.float32), np.ones((0, 1)), 1.0,
+                         precision="bf16")
+    assert out.shape == (5, 1) and not out.any()
+
+
+def test_large_c2_shape_row_subset():
+    """Configuration-2 shape (N=200k, d=64): 512 seeded rows vs the oracle over all of K.
+
+    Exercises the persistent schedule with row tiles cut between CTAs."""
+    from flashdiffusion_b200 import synthetic, GaussianOperator
+    from flashdiffusion_b200.kernel_cuda_sm100 import normalise
+    X, beta = synthetic.gaussian_mixture(n=200_000, d=64, seed=0)
+    op = GaussianOperator(X, None, beta, "bf16")
+    v = np.random.default_rng(1).standard_normal(X.shape[0])
+    vd = torch.from_numpy(v).cuda()
+    out = op.apply(vd, out_dtype=torch.float64)[:, 0].cpu().numpy()
+    rows = np.sort(np.random.default_rng(2).choice(X.shape[0], 512, replace=False))
+    ref = O.flash_diffusion(X[rows], X, v[:, None], beta)[:, 0]
+    assert rel_l2(out[rows], ref) <= TOL["bf16"]
+    # deterministic: a second launch is bit-identical
+    out2 = op.apply(vd, out_dtype=torch.float64)[:, 0].cpu().numpy()
+    assert np.array_equal(out, out2)
+    D, Da, rs = normalise(op, 0.5)
+    Dref = O.prepass_rowsum(X[rows], X, beta)
+    assert rel_l2(D.double().cpu().numpy()[rows], Dref) <= TOL["bf16"]
+
+
+def test_reference_module_contract():
+    """flash_diffusion_sm100.{compute_sq_norms, prepass, matvec} — FD/csrc/flash_diffusion_sm100.cu:456-588."""
+    from flashdiffusion_b200 import flash_diffusion_sm100 as ext
+    from tests.golden.make_golden import test_roll
+    X = test_roll(150)
+    beta, alpha = 1.0, 0.5
+    Xh = torch.from_numpy(X.astype(np.float16)).cuda()
+    sq = ext.compute_sq_norms(Xh)
+    np.testing.assert_allclose(sq.cpu().numpy(), (X.astype(np.float16).astype(np.float32) ** 2).sum(1), rtol=1e-5)
+    ones = torch.ones(150, dtype=torch.float32, device="cuda")
+    D = ext.prepass(Xh, ones, sq, beta)
+    Xr = X.astype(np.float16).astype(np.float64)
+    M, rs = O.dense_dmap_operator(Xr, beta, alpha)
+    assert rel_l2(D.cpu().numpy(), O.dense_kernel(Xr, beta).sum(1)) <= 2e-3
+    v = np.random.default_rng(7).standard_normal(150)
+    out = ext.matvec(Xh, torch.from_numpy(v.astype(np.float32)).cuda(), torch.from_numpy(rs.astype(np.float32)).cuda(),
+                     sq, beta)
+    assert rel_l2(out.cpu().numpy(), M @ v) <= 2e-3
+    with pytest.raises(RuntimeError, match="must be CUDA"):
+        ext.compute_sq_norms(Xh.cpu())
+    with pytest.raises(RuntimeError, match="2D"):
+        ext.compute_sq_norms(Xh[:, 0].contiguous())
+    with pytest.raises(RuntimeError, match="length must equal N"):
+        ext.prepass(Xh, ones[:10], sq, beta)
+    with pytest.raises(RuntimeError, match="float32"):
+        ext.prepass(Xh, ones.double(), sq, beta)
+
+
+def test_backend_contract():
+    """_get_cuda_backend -> (precompute_sm100, matvec_sm100) as in FD/kernel.py:68-118."""
+    from flashdiffusion_b200 import _get_cuda_backend
+    from tests.golden.make_golden import test_roll
+    pre, mv = _get_cuda_backend()
+    X = test_roll(150)
+    st = pre(X, 1.0, 0.5)
+    for name in ("D", "D_alpha", "rscale"):
+        assert getattr(st, name).is_cuda
+    M, rs = O.dense_dmap_operator(X, 1.0, 0.5)
+    v = np.random.default_rng(0).standard_normal(150)
+    out = mv(st, v)
+    assert out.dtype == np.float64
+    assert rel_l2(out, M @ v) <= 2e-3
