@@ -32,7 +32,7 @@ int launch_zero_rows(int64_t nq, int rc, const RowEpilogue& ep, cudaStream_t s) 
 }
 
 static bool valid_dtype(int t) { return t == FD_DTYPE_F32 || t == FD_DTYPE_F16 || t == FD_DTYPE_BF16 || t == FD_DTYPE_F64; }
-static bool valid_tile(int t) { return t == FD_TILE_BF16 || t == FD_TILE_F32; }
+static bool valid_tile(int t) { return t == FD_TILE_BF16 || t == FD_TILE_F32 || t == FD_TILE_F16; }
 
 // columns of V handled per tile-kernel launch
 static int cols_per_launch(int tile) { return tile == FD_TILE_F32 ? 64 : 1; }
@@ -146,8 +146,7 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
             // the fp32 operands carry sqrt(beta) in their coordinates
             FD_TRY(launch_simt(qp, qsq, nq, kp, ksq, nk, d, u, rc, 1.0f, ep, kws, kws_bytes, s));
         } else {
-            FD_TRY(launch_tc((const __nv_bfloat16*)Qop, nq, (const __nv_bfloat16*)Kop, nk, d, u, rc, ep, kws,
-                             kws_bytes, s));
+            FD_TRY(launch_tc(Qop, nq, Kop, nk, d, tile, u, rc, ep, kws, kws_bytes, s));
         }
     }
     return FD_OK;

@@ -47,12 +47,16 @@ __device__ __forceinline__ double load_as_f64(const void* p, int dtype, int64_t 
 }
 
 // ---- operand formats -------------------------------------------------------
-// FD_TILE_BF16 operand ("packed bf16 row"): row-major [n][kd] bf16 with
-//   query row  q~ = [ c*(x-shift) rounded to bf16 (d) | 1 1 1 | split3(nq) | 0 pad ]
-//   key   row  k~ = [ (x-shift) rounded to bf16 (d)   | split3(nk) | 1 1 1 | 0 pad ]
-// with c = 2*beta*log2(e), nq = -||q^||^2/(2c) ... so that q~.k~ equals the
-// base-2 exponent -beta*log2(e)*||a-b||^2 of the two rounded points (a = q^/c, b).
-// kd = round_up(d + 6, 16).  Everything else (norms, bias) is folded in.
+// 16-bit tile operand (FD_TILE_F16 / FD_TILE_BF16): row-major [n][kd] of
+// fp16 / bf16 with s = sqrt(2*beta*log2(e)) and a^ = round16(s*(x-shift)):
+//   query row  q~ = [ a^ (d) | 1 1 1 | split3(n) | 0 pad ]
+//   key   row  k~ = [ a^ (d) | split3(n) | 1 1 1 | 0 pad ]
+// n = -||a^||^2 / 2 of the row's own rounded values (split3 = three 16-bit
+// parts summing to n to ~2^-24 relative).  Then q~.k~ = -(1/2)||a^_q - a^_k||^2
+// = -beta*log2(e)*||a_q - a_k||^2 exactly for the rounded points a = a^/s:
+// one MMA accumulator element is the whole base-2 exponent of a pair, and
+// both sides round identically, so K(i,j) = K(j,i) for Q = K.
+// kd = round_up(d + 6, 16).
 //
 // FD_TILE_F32 operand: row-major [n][dp] fp32 centred points scaled by
 // sqrt(beta), dp = round_up(d,4), followed by n fp32 squared norms of the

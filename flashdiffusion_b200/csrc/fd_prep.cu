@@ -32,50 +32,64 @@ __global__ void mean_rows_kernel(const void* __restrict__ X, int dtype, int64_t 
     }
 }
 
-__device__ __forceinline__ void split3(double x, __nv_bfloat16& hi, __nv_bfloat16& mid,
-                                       __nv_bfloat16& lo) {
-    hi = __double2bfloat16(x);
-    const double r1 = x - (double)__bfloat162float(hi);
-    mid = __double2bfloat16(r1);
-    const double r2 = r1 - (double)__bfloat162float(mid);
-    lo = __double2bfloat16(r2);
-}
+// 16-bit element conversion helpers (round to nearest)
+struct H16 {
+    typedef __half T;
+    static __device__ __forceinline__ T from(double x) { return __float2half_rn((float)x); }
+    static __device__ __forceinline__ double to(T v) { return (double)__half2float(v); }
+    static constexpr double kMax = 65504.0;
+};
+struct B16 {
+    typedef __nv_bfloat16 T;
+    static __device__ __forceinline__ T from(double x) { return __double2bfloat16(x); }
+    static __device__ __forceinline__ double to(T v) { return (double)__bfloat162float(v); }
+    static constexpr double kMax = 3.0e38;
+};
 
-// Packed bf16 operand (layout documented in fd_common.cuh).  One warp per row.
-__global__ void pack_bf16_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
-                                 const float* __restrict__ shift, double c2, int side, int kd,
-                                 __nv_bfloat16* __restrict__ out) {
+// Packed 16-bit operand (layout documented in fd_common.cuh).  One warp per
+// row.  When a value of the row exceeds the 16-bit range, FD_ERR_RANGE is
+// recorded in *status (the caller then repacks with the wider bf16 format).
+template <class F>
+__global__ void pack16_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                              const float* __restrict__ shift, double s, int side, int kd,
+                              typename F::T* __restrict__ out, int* __restrict__ status) {
+    typedef typename F::T T;
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x & 31;
     if (row >= n) return;
-    __nv_bfloat16* o = out + row * kd;
-    const double scale = side == FD_SIDE_QUERY ? c2 : 1.0;
-    double ss = 0.0;
+    T* o = out + row * kd;
+    double ss = 0.0, amax = 0.0;
     for (int k = lane; k < d; k += 32) {
         double x = load_as_f64(X, dtype, row * d + k);
         if (shift) x -= (double)shift[k];
-        const __nv_bfloat16 b = __double2bfloat16(x * scale);
-        const double bv = (double)__bfloat162float(b);
+        const T b = F::from(x * s);
+        const double bv = F::to(b);
         ss += bv * bv;
+        amax = fmax(amax, fabs(x * s));
         o[k] = b;
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    for (int off = 16; off > 0; off >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        amax = fmax(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    }
     if (lane == 0) {
-        // query: nq = -||q^||^2 / (2 c2); key: nk = -(c2/2) ||b||^2
-        const double nrm = side == FD_SIDE_QUERY ? -ss / (2.0 * c2) : -0.5 * c2 * ss;
-        __nv_bfloat16 h, m, l;
-        split3(nrm, h, m, l);
-        const __nv_bfloat16 one = __float2bfloat16(1.0f);
+        const double nrm = -0.5 * ss;
+        const T hi = F::from(nrm);
+        const double r1 = nrm - F::to(hi);
+        const T mid = F::from(r1);
+        const T lo = F::from(r1 - F::to(mid));
+        if (amax > 0.99 * F::kMax || -nrm > 0.99 * F::kMax || !(ss == ss)) atomicExch(status, FD_ERR_RANGE);
+        const T one = F::from(1.0);
         if (side == FD_SIDE_QUERY) {
             o[d + 0] = one; o[d + 1] = one; o[d + 2] = one;
-            o[d + 3] = h; o[d + 4] = m; o[d + 5] = l;
+            o[d + 3] = hi; o[d + 4] = mid; o[d + 5] = lo;
         } else {
-            o[d + 0] = h; o[d + 1] = m; o[d + 2] = l;
+            o[d + 0] = hi; o[d + 1] = mid; o[d + 2] = lo;
             o[d + 3] = one; o[d + 4] = one; o[d + 5] = one;
         }
     }
-    for (int k = d + 6 + lane; k < kd; k += 32) o[k] = __float2bfloat16(0.0f);
+    for (int k = d + 6 + lane; k < kd; k += 32) o[k] = F::from(0.0);
 }
 
 // fp32 operand: centred points scaled by sqrt(beta) [n][dp], then n squared
@@ -186,10 +200,16 @@ int launch_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, c
 int launch_pack(const void* X, int dtype, int64_t n, int d, const float* shift, float beta, int side,
                 int tile, void* op, cudaStream_t s) {
     if (n == 0) return FD_OK;
-    if (tile == FD_TILE_BF16) {
-        const double c2 = 2.0 * (double)beta * 1.4426950408889634;  // 2 beta log2(e)
-        pack_bf16_kernel<<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, c2, side, kd_bf16(d),
-                                                       (__nv_bfloat16*)op);
+    if (tile == FD_TILE_BF16 || tile == FD_TILE_F16) {
+        const double sc = sqrt(2.0 * (double)beta * 1.4426950408889634);  // sqrt(2 beta log2(e))
+        int* status = nullptr;
+        FD_TRY(status_word(&status));
+        if (tile == FD_TILE_F16)
+            pack16_kernel<H16><<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, sc, side, kd_bf16(d),
+                                                             (__half*)op, status);
+        else
+            pack16_kernel<B16><<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, sc, side, kd_bf16(d),
+                                                             (__nv_bfloat16*)op, status);
     } else {
         const int dp = dp_f32(d);
         float* pts = (float*)op;

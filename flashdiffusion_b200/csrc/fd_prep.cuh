@@ -44,11 +44,14 @@ int launch_simt(const float* qpts, const float* qsq, int64_t nq, const float* kp
                 int64_t nk, int d, const float* u, int rc, float beta, const RowEpilogue& ep,
                 void* ws, size_t ws_bytes, cudaStream_t s);
 
-// bf16 tcgen05 tiles (FD_TILE_BF16).
+// 16-bit tcgen05 tiles (FD_TILE_F16 / FD_TILE_BF16).
 size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc);
-int launch_tc(const __nv_bfloat16* qop, int64_t nq, const __nv_bfloat16* kop, int64_t nk, int d,
+int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
               const void* rhs, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes, cudaStream_t s);
 
 int read_and_clear_status(cudaStream_t s, int* status);
+// Device address of the library's status word (bounded-wait timeouts, fp16 range).
+int status_word(int** ptr);
+static inline bool is_tc_tile(int tile) { return tile == FD_TILE_BF16 || tile == FD_TILE_F16; }
 
 }  // namespace fd

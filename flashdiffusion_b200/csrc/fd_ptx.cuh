@@ -93,7 +93,7 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D(tmem) (+)= A(smem desc) * B(smem desc)^T, bf16 inputs, fp32 accumulate.
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, 16-bit inputs, fp32 accumulate.
 __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                         uint32_t accumulate) {
     asm volatile(
@@ -127,9 +127,11 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::f16: bf16 A and B (both K-major), fp32 D, MxN.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor, kind::f16: A and B of the same 16-bit type (fp16
+// when f16, else bf16), both K-major, fp32 D, shape MxN.
+__host__ __device__ constexpr uint32_t idesc_f32acc(int M, int N, bool f16) {
+    return (1u << 4) | ((f16 ? 0u : 1u) << 7) | ((f16 ? 0u : 1u) << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
 }
 
 // 32 lanes x 32 consecutive 32-bit columns -> 32 registers per thread.

@@ -1,4 +1,4 @@
-// bf16 tensor-core path (FD_TILE_BF16) of the Gaussian-kernel operator on
+// 16-bit tensor-core path (FD_TILE_F16 / FD_TILE_BF16) of the Gaussian-kernel operator on
 // sm_100a: a persistent, warp-specialised kernel.
 //
 //   out_i = ep_i * sum_j 2^( q~_i . k~_j ) * u_j          (q~.k~ <= 0 up to rounding)
@@ -68,7 +68,7 @@ __device__ __forceinline__ bool seg_end(int64_t n, int64_t n1, int64_t n_jt) {
 template <int KB>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-          const float* __restrict__ u, int64_t nq, int kd, Sched sc, RowEpilogue ep,
+          const float* __restrict__ u, int64_t nq, int kd, uint32_t idesc, Sched sc, RowEpilogue ep,
           double* __restrict__ part) {
     using C = Cfg<KB>;
     extern __shared__ uint8_t smem_raw[];
@@ -155,7 +155,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
         }
     } else if (warp == MMA_WARP) {
         if (lane == 0) {
-            constexpr uint32_t idesc = ptx::idesc_bf16_f32(BM, BN);
             const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
@@ -317,7 +316,7 @@ static int get_encode(EncodeTiledFn* fn) {
 }
 
 // 2-D bf16 map over a [rows][cols] row-major matrix, 64 x box_rows boxes, 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16) {
     EncodeTiledFn enc;
     FD_TRY(get_encode(&enc));
     FD_CHECK_ARG(((uintptr_t)ptr & 15) == 0, "tile operand must be 16-byte aligned");
@@ -326,7 +325,7 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
     cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
     cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+    CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -346,28 +345,30 @@ size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
 
 template <int KB>
 static int launch_tc_kb(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
-                        const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
+                        uint32_t idesc, const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
     using C = tc::Cfg<KB>;
     FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
-    tc::tc_kernel<KB><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, sc, ep, part);
+    tc::tc_kernel<KB><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
 
-int launch_tc(const __nv_bfloat16* qop, int64_t nq, const __nv_bfloat16* kop, int64_t nk, int d,
+int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
               const void* rhs, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes, cudaStream_t s) {
     if (nq == 0) return FD_OK;
     if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
-    if (rc != 1) return set_error(FD_ERR_UNSUPPORTED, "bf16 tile path: block right-hand sides not built yet");
+    if (rc != 1) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path: block right-hand sides not built yet");
     const int kd = kd_bf16(d);
     const int kb = (int)cdiv(kd, 64);
-    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "bf16 tile path supports d <= 186 (got d=%d)", d);
+    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path supports d <= 186 (got d=%d)", d);
     const size_t need = tc_workspace_bytes(nq, nk, rc);
-    if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "bf16 tile path: workspace %zu B < %zu B", ws_bytes, need);
+    if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "16-bit tile path: workspace %zu B < %zu B", ws_bytes, need);
     CUtensorMap mq, mk;
-    FD_TRY(make_map(&mq, qop, nq, kd, tc::BM));
-    FD_TRY(make_map(&mk, kop, nk, kd, tc::BN));
+    const bool f16 = tile == FD_TILE_F16;
+    FD_TRY(make_map(&mq, qop, nq, kd, tc::BM, f16));
+    FD_TRY(make_map(&mk, kop, nk, kd, tc::BN, f16));
+    const uint32_t idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
     tc::Sched sc;
     sc.n_jt = cdiv(nk, tc::BN);
     sc.units = cdiv(nq, tc::ROWS) * sc.n_jt;
@@ -375,12 +376,22 @@ int launch_tc(const __nv_bfloat16* qop, int64_t nq, const __nv_bfloat16* kop, in
     double* part = (double*)ws;
     const float* u = (const float*)rhs;
     switch (kb) {
-        case 1: FD_TRY(launch_tc_kb<1>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
-        case 2: FD_TRY(launch_tc_kb<2>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
-        default: FD_TRY(launch_tc_kb<3>(mq, mk, u, nq, kd, sc, ep, part, s)); break;
+        case 1: FD_TRY(launch_tc_kb<1>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+        case 2: FD_TRY(launch_tc_kb<2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+        default: FD_TRY(launch_tc_kb<3>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
     }
     tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(part, sc, nq, ep);
     FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int status_word(int** ptr) {
+    static int* cached[64] = {nullptr};
+    int dev = 0;
+    FD_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(FD_ERR_ARG, "device index %d out of range", dev);
+    if (!cached[dev]) FD_CUDA_TRY(cudaGetSymbolAddress((void**)&cached[dev], g_fd_status));
+    *ptr = cached[dev];
     return FD_OK;
 }
 

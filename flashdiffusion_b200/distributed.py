@@ -67,7 +67,7 @@ class ShardedDMAP:
     a host fake in tests.
     """
 
-    def __init__(self, X: torch.Tensor, beta: float, alpha: float, precision: str = "bf16", group=None,
+    def __init__(self, X: torch.Tensor, beta: float, alpha: float, precision: str = "f16", group=None,
                  local_apply: Optional[Callable] = None):
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0

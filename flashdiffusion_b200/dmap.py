@@ -11,8 +11,8 @@ Drop-in for ``FD/dmap.py`` of the reference:
   ``matvec(v) = M (h v) / Ph`` — here on the GPU with the division fused into
   the tile epilogue (the reference always runs it in NumPy).
 
-Extra keyword ``precision`` ("ramp" default, "bf16", "fp32"): "ramp" fits and
-starts the eigensolver on bf16 tensor-core tiles, then finishes on fp32 tiles
+Extra keyword ``precision`` ("ramp" default, "f16", "bf16", "fp32"): "ramp"
+fits and starts the eigensolver on 16-bit tensor-core tiles, then finishes on fp32 tiles
 with an fp64 Rayleigh-Ritz (the precision ramp the reference's docstrings
 describe, ``FD/eigensolver.py:15-23``); after ``transform`` the fitted mirrors
 hold the fp32 normalisation.
@@ -37,8 +37,8 @@ class DiffusionMap:
 
     def __init__(self, beta: float = 1.0, alpha: float = 0.5, n_components: int = 8, tile: int = 512,
                  precision: str = "ramp", verbose: bool = False):
-        if precision not in ("ramp", "bf16", "fp32"):
-            raise ValueError(f"precision must be 'ramp', 'bf16' or 'fp32' (got {precision!r})")
+        if precision not in ("ramp", "f16", "bf16", "fp32"):
+            raise ValueError(f"precision must be 'ramp', 'f16', 'bf16' or 'fp32' (got {precision!r})")
         self.beta = beta
         self.alpha = alpha
         self.n_components = n_components
@@ -76,7 +76,7 @@ class DiffusionMap:
         """Two prepass reductions on the GPU: D, w = D^-alpha, D_alpha, rscale."""
         self.X_ = np.asarray(X, dtype=np.float64) if not isinstance(X, torch.Tensor) else None
         self._Xd = to_device(X, torch.float32)
-        first = "bf16" if self.precision == "ramp" else self.precision
+        first = "f16" if self.precision == "ramp" else self.precision
         self._cuda_state = self._state(first)
         self._hi_state = self._cuda_state if self.precision == "fp32" else None
         self.timings_["fit_s"] = self._cuda_state.timings["precompute_s"]

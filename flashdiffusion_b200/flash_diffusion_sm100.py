@@ -8,7 +8,8 @@ libfd_sm100's C ABI (``fd_compute_sq_norms``, ``fd_prepass``, ``fd_matvec``).
 
 Differences, by design: X may be float16, bfloat16 or float32 (the reference
 accepts float16 only); the kernels evaluate distances from their own rounded
-bf16 operands, so ``sq_X`` is checked for shape but not read.
+fp16 tile operands (norms folded into the operand), so ``sq_X`` is checked for
+shape but not read.
 """
 
 from __future__ import annotations
@@ -44,7 +45,7 @@ def _check_vec(x, n, name):
 
 def _ws(n, d):
     lib = native.load()
-    nbytes = int(lib.fd_workspace_bytes(n, n, d, 1, native.TILE_BF16))
+    nbytes = int(lib.fd_workspace_bytes(n, n, d, 1, native.TILE_F16))
     return native.workspace.get(nbytes, torch.device("cuda", torch.cuda.current_device()))
 
 
@@ -65,7 +66,7 @@ def prepass(X_fp16: torch.Tensor, w: torch.Tensor, sq_X: torch.Tensor, beta: flo
     D = torch.empty(n, dtype=torch.float32, device=X_fp16.device)
     ws = _ws(n, d)
     native.check(native.load().fd_prepass(native._ptr(X_fp16), native._TORCH_DTYPE[X_fp16.dtype], n, d,
-                                          native._ptr(w), float(beta), native.TILE_BF16, native._ptr(D),
+                                          native._ptr(w), float(beta), native.TILE_F16, native._ptr(D),
                                           native._ptr(ws), ws.numel(), native._stream(X_fp16.device)))
     return D
 
@@ -80,7 +81,7 @@ def matvec(X_fp16: torch.Tensor, v: torch.Tensor, rscale: torch.Tensor, sq_X: to
     out = torch.empty(n, dtype=torch.float32, device=X_fp16.device)
     ws = _ws(n, d)
     native.check(native.load().fd_matvec(native._ptr(X_fp16), native._TORCH_DTYPE[X_fp16.dtype], n, d,
-                                         native._ptr(v), native._ptr(rscale), float(beta), native.TILE_BF16,
+                                         native._ptr(v), native._ptr(rscale), float(beta), native.TILE_F16,
                                          native._ptr(out), native._ptr(ws), ws.numel(),
                                          native._stream(X_fp16.device)))
     return out

@@ -17,8 +17,10 @@ materialised.  The reference's ``tile`` argument (host tile size) is accepted
 for compatibility; device tile shapes are fixed by the kernels.
 ``coord_dtype`` selects the tile precision: ``np.float32`` (the reference
 default) runs fp32 tiles (relative error ~1e-6, the reference's own class),
-``np.float16``/bfloat16 run the tensor-core bf16 tiles (relative L2 error
-<= 2e-3).  ``precision="bf16"|"fp32"`` overrides it.  NumPy inputs give NumPy
+``np.float16`` runs the tcgen05 tensor-core tiles with fp16 operands (relative
+L2 error <= 2e-3; bf16 operands are used automatically when a point lies too
+far from the data mean for the fp16 range), bfloat16 forces bf16 operands.
+``precision="f16"|"bf16"|"fp32"`` overrides it.  NumPy inputs give NumPy
 outputs of ``accum_dtype``; CUDA tensor inputs give CUDA tensors.
 """
 
@@ -34,7 +36,7 @@ from . import native
 # SM -> kernel family.  This build ships the B200 family only.
 _SM_BACKEND = {100: "sm100", 103: "sm100"}
 
-TILE_NAMES = {"bf16": native.TILE_BF16, "fp32": native.TILE_F32}
+TILE_NAMES = {"f16": native.TILE_F16, "bf16": native.TILE_BF16, "fp32": native.TILE_F32}
 
 
 def _cuda_sm() -> Optional[int]:
@@ -67,10 +69,15 @@ def tile_of(precision=None, coord_dtype=np.float32) -> int:
         if precision not in TILE_NAMES:
             raise ValueError(f"precision must be one of {sorted(TILE_NAMES)} (got {precision!r})")
         return TILE_NAMES[precision]
-    cd = np.dtype(coord_dtype) if not isinstance(coord_dtype, torch.dtype) else coord_dtype
-    if cd in (np.dtype(np.float16), torch.float16, torch.bfloat16):
+    if coord_dtype is torch.bfloat16:
         return native.TILE_BF16
+    cd = np.dtype(coord_dtype) if not isinstance(coord_dtype, torch.dtype) else coord_dtype
+    if cd in (np.dtype(np.float16), torch.float16):
+        return native.TILE_F16
     return native.TILE_F32
+
+
+PREC_OF_TILE = {v: k for k, v in TILE_NAMES.items()}
 
 
 def to_device(x, dtype=None, device=None) -> Optional[torch.Tensor]:
@@ -97,7 +104,7 @@ class GaussianOperator:
     invariant so the operator is unchanged.
     """
 
-    def __init__(self, Q, K=None, beta: float = 1.0, precision: str = "bf16", device=None, shift=None):
+    def __init__(self, Q, K=None, beta: float = 1.0, precision: str = "f16", device=None, shift=None):
         self.device = native.require_device(device)
         Qd = to_device(Q, device=self.device)
         Kd = Qd if K is None else to_device(K, device=self.device)
@@ -111,8 +118,20 @@ class GaussianOperator:
         self.nq, self.d = Qd.shape
         self.nk = Kd.shape[0]
         self.shift = native.mean_rows(Kd) if shift is None else shift
-        self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)
-        self.kop = native.pack(Kd, self.beta, native.SIDE_KEY, self.tile, self.shift)
+        if self.tile == native.TILE_F16:
+            # fp16 operands unless some packed value would leave the fp16 range
+            native.check_status(self.device)
+            self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)
+            self.kop = native.pack(Kd, self.beta, native.SIDE_KEY, self.tile, self.shift)
+            try:
+                native.check_status(self.device)
+            except native.FDError as e:
+                if e.code != native.FD_ERR_RANGE:
+                    raise
+                self.tile, self.precision = native.TILE_BF16, "bf16"
+        if self.tile != native.TILE_F16:
+            self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)
+            self.kop = native.pack(Kd, self.beta, native.SIDE_KEY, self.tile, self.shift)
         self.symmetric = K is None
 
     def apply(self, V=None, col_scale=None, col_h=None, row_scale=None, row_div=None,
@@ -138,7 +157,7 @@ def prepass_rowsum(Q, K, beta: float, weights_k=None, tile: int = 512, precision
     Returns (N_q,) float64 (NumPy for NumPy inputs, CUDA tensor otherwise).
     """
     numpy_io = not isinstance(Q, torch.Tensor)
-    op = GaussianOperator(Q, None if K is Q else K, beta, "bf16" if tile_of(precision, coord_dtype) == 0 else "fp32")
+    op = GaussianOperator(Q, None if K is Q else K, beta, PREC_OF_TILE[tile_of(precision, coord_dtype)])
     w = _f32(weights_k, op.device)
     out = op.apply(w, out_dtype=torch.float64)[:, 0]
     return out.cpu().numpy() if numpy_io else out
@@ -158,7 +177,7 @@ def FlashDiffusion(Q, K, V, beta: float, rscale_q=None, rscale_k=None, h=None, t
     each output row (the Doob normaliser, ``FD/dmap.py:249-261``).
     """
     numpy_io = not isinstance(Q, torch.Tensor)
-    prec = "bf16" if tile_of(precision, coord_dtype) == native.TILE_BF16 else "fp32"
+    prec = PREC_OF_TILE[tile_of(precision, coord_dtype)]
     same = K is Q
     op = GaussianOperator(Q, None if same else K, beta, prec)
     dev = op.device

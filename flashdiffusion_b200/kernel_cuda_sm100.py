@@ -7,9 +7,9 @@ two Coifman-Lafon prepasses on the GPU and returns a state whose ``.D``,
 ``.D_alpha`` and ``.rscale`` are CUDA tensors; ``matvec_sm100(state, v)``
 applies M = diag(rscale) K diag(rscale) to a NumPy vector and returns float64.
 
-The kernels are this package's sm_100a tcgen05 tiles (bf16 operands, fp32
-accumulation) instead of the reference's WMMA fp16 kernel; ``precision="fp32"``
-selects the fp32 tiles.
+The kernels are this package's sm_100a tcgen05 tiles (fp16 operands like the
+reference's X_fp16, fp32 accumulation) instead of the reference's WMMA
+kernel; ``precision="fp32"`` selects the fp32 tiles.
 """
 
 from __future__ import annotations
@@ -55,7 +55,7 @@ def normalise(op: GaussianOperator, alpha: float):
     return D, D_alpha, rscale
 
 
-def precompute_sm100(X, beta: float, alpha: float = 0.5, precision: str = "bf16") -> CUDAStateSM100:
+def precompute_sm100(X, beta: float, alpha: float = 0.5, precision: str = "f16") -> CUDAStateSM100:
     """Two-pass Coifman-Lafon precomputation on the GPU."""
     Xd = to_device(X)
     op = GaussianOperator(Xd, None, beta, precision)

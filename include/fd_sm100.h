@@ -40,6 +40,7 @@ extern "C" {
 #define FD_ERR_UNSUPPORTED 3  /* device is not sm_100-family or shape unsupported     */
 #define FD_ERR_TIMEOUT 4      /* a bounded device-side wait gave up                   */
 #define FD_ERR_WORKSPACE 5    /* caller workspace too small                           */
+#define FD_ERR_RANGE 6        /* fp16 tile operand would overflow (use FD_TILE_BF16)   */
 
 /* element types of caller inputs */
 #define FD_DTYPE_F32 0
@@ -48,8 +49,11 @@ extern "C" {
 #define FD_DTYPE_F64 3
 
 /* tile precision of the distance GEMM */
-#define FD_TILE_BF16 0  /* tcgen05 bf16 tiles, fp32 accumulation (matvec rel. L2 <= 2e-3) */
-#define FD_TILE_F32 1   /* fp32 tiles (rel. L2 <= 1e-5)                                  */
+#define FD_TILE_BF16 0  /* tcgen05 16-bit tiles, bf16 operands (wide range), fp32 accumulation */
+#define FD_TILE_F32 1   /* fp32 SIMT tiles (matvec rel. L2 <= 1e-5)                           */
+#define FD_TILE_F16 2   /* tcgen05 16-bit tiles, fp16 operands, fp32 accumulation: same speed
+                           as bf16 with 8x finer rounding (matvec rel. L2 <= 2e-3); packing
+                           records FD_ERR_RANGE in the status word when a row would overflow */
 
 /* operand side for fd_pack_operand */
 #define FD_SIDE_QUERY 0
@@ -64,15 +68,15 @@ int fd_version(void);
 /* 1 if `device` is a compute-capability 10.x (B200-class) GPU, else 0. */
 int fd_device_supported(int device);
 
-/* Read and clear the device status word written by bounded waits
- * (FD_OK or FD_ERR_TIMEOUT).  Synchronises `stream`. */
+/* Read and clear the device status word written by bounded waits and by
+ * fp16 packing (FD_OK, FD_ERR_TIMEOUT or FD_ERR_RANGE).  Synchronises `stream`. */
 int fd_check_status(void* stream);
 
 /* ---------------------------------------------------------------------------
  * Reference-compatible trio.  Replaces the pybind module flash_diffusion_sm100
  * (FD/csrc/flash_diffusion_sm100.cu:571-588) as used by FD/kernel_cuda_sm100.py:67-119.
- * X is (n, d) row-major of dtype FD_DTYPE_*.  `tile` selects FD_TILE_BF16 or
- * FD_TILE_F32.  Workspace: fd_workspace_bytes(n, n, d, 1, tile).
+ * X is (n, d) row-major of dtype FD_DTYPE_*.  `tile` selects FD_TILE_F16,
+ * FD_TILE_BF16 or FD_TILE_F32.  Workspace: fd_workspace_bytes(n, n, d, 1, tile).
  * ------------------------------------------------------------------------- */
 
 /* sq[i] = sum_k X[i,k]^2 in fp32.  Replaces compute_sq_norms

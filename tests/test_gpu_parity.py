@@ -1,8 +1,11 @@
 """GPU parity of the sm_100a kernels against the pinned CPU oracle / reference goldens.
 
-Tolerances: matvec relative L2 error <= 2e-3 with bf16
-tiles and <= 1e-5 with fp32 tiles; eigenvalues within 1e-6 relative after the
-fp64 ramp.  Everything here goes through the C ABI of libfd_sm100.so.
+Tolerances: matvec relative L2 error <= 2e-3 with the
+16-bit tensor-core tiles (default fp16 operands) and <= 1e-5 with fp32 tiles;
+eigenvalues within 1e-6 relative after the fp64 ramp.  The bf16-operand
+variant (kept for data whose packed values leave the fp16 range) rounds 8x
+more coarsely and is held to 4e-3.  Everything here goes through the C ABI of
+libfd_sm100.so.
 """
 import numpy as np
 import pytest
@@ -12,7 +15,7 @@ from oracle import fd_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"bf16": 2e-3, "fp32": 1e-5}
+TOL = {"f16": 2e-3, "bf16": 4e-3, "fp32": 1e-5}
 
 
 def rel_l2(a, b):
@@ -29,7 +32,7 @@ def _lib():
     native.check_status()
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 def test_prepass_golden(gold, prec):
     from flashdiffusion_b200 import prepass_rowsum
     g = gold("prepass.npz")
@@ -40,7 +43,7 @@ def test_prepass_golden(gold, prec):
         np.testing.assert_allclose(prepass_rowsum(X, X, 1.0, precision=prec), g["D64"], rtol=1e-5)
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 @pytest.mark.parametrize("n", [0, 1, 2])
 def test_dmap_matvec_golden(gold, prec, n):
     from flashdiffusion_b200 import FlashDiffusion
@@ -53,7 +56,7 @@ def test_dmap_matvec_golden(gold, prec, n):
         np.testing.assert_allclose(out, g[f"out{n}"], rtol=2e-4, atol=1e-10)
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 def test_amap_block_golden(gold, prec):
     """Q != K, separate rscale_q / rscale_k, Doob h, r = 3 columns."""
     from flashdiffusion_b200 import FlashDiffusion
@@ -66,7 +69,7 @@ def test_amap_block_golden(gold, prec):
     assert rel_l2(plain, g["out_plain"]) <= TOL[prec]
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 def test_gmm64_fit_and_matvec_golden(gold, prec):
     from flashdiffusion_b200 import DiffusionMap
     g = gold("gmm64.npz")
@@ -76,7 +79,7 @@ def test_gmm64_fit_and_matvec_golden(gold, prec):
     assert rel_l2(dm.matvec(g["v"]), g["out"]) <= 2 * TOL[prec]
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 def test_doob_golden(gold, prec):
     from flashdiffusion_b200 import DiffusionMap
     g = gold("doob.npz")
@@ -129,7 +132,7 @@ def test_nystrom_golden(gold):
     assert rel_l2(c, g["coords"]) <= 1e-5
 
 
-@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
 @pytest.mark.parametrize("nq,nk,d,r", [(1, 1, 3, 1), (129, 257, 3, 1), (300, 200, 64, 1), (257, 511, 66, 1),
                                        (200, 1000, 128, 1), (130, 700, 186, 1), (70, 90, 5, 4),
                                        (513, 300, 64, 2)])
@@ -161,19 +164,19 @@ def test_large_c2_shape_row_subset():
     from flashdiffusion_b200 import synthetic, GaussianOperator
     from flashdiffusion_b200.kernel_cuda_sm100 import normalise
     X, beta = synthetic.gaussian_mixture(n=200_000, d=64, seed=0)
-    op = GaussianOperator(X, None, beta, "bf16")
+    op = GaussianOperator(X, None, beta, "f16")
     v = np.random.default_rng(1).standard_normal(X.shape[0])
     vd = torch.from_numpy(v).cuda()
     out = op.apply(vd, out_dtype=torch.float64)[:, 0].cpu().numpy()
     rows = np.sort(np.random.default_rng(2).choice(X.shape[0], 512, replace=False))
     ref = O.flash_diffusion(X[rows], X, v[:, None], beta)[:, 0]
-    assert rel_l2(out[rows], ref) <= TOL["bf16"]
+    assert rel_l2(out[rows], ref) <= TOL["f16"]
     # deterministic: a second launch is bit-identical
     out2 = op.apply(vd, out_dtype=torch.float64)[:, 0].cpu().numpy()
     assert np.array_equal(out, out2)
     D, Da, rs = normalise(op, 0.5)
     Dref = O.prepass_rowsum(X[rows], X, beta)
-    assert rel_l2(D.double().cpu().numpy()[rows], Dref) <= TOL["bf16"]
+    assert rel_l2(D.double().cpu().numpy()[rows], Dref) <= TOL["f16"]
 
 
 def test_reference_module_contract():
