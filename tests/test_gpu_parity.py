@@ -4,7 +4,10 @@ Tolerances: matvec relative L2 error <= 2e-3 with the
 16-bit tensor-core tiles (default fp16 operands) and <= 1e-5 with fp32 tiles;
 eigenvalues within 1e-6 relative after the fp64 ramp.  The bf16-operand
 variant (kept for data whose packed values leave the fp16 range) rounds 8x
-more coarsely and is held to 4e-3.  Everything here goes through the C ABI of
+more coarsely and is held to 1e-2.  Where the reference algorithm itself
+(fp32 distances of uncentred coordinates) strays from the exact answer, the
+kernels are held to the tolerance against an exact fp64 dense evaluation and
+to the tolerance plus the reference's own measured error against the oracle.  Everything here goes through the C ABI of
 libfd_sm100.so.
 """
 import numpy as np
@@ -15,13 +18,27 @@ from oracle import fd_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"f16": 2e-3, "bf16": 4e-3, "fp32": 1e-5}
+TOL = {"f16": 2e-3, "bf16": 1e-2, "fp32": 1e-5}
 
 
 def rel_l2(a, b):
     a = np.asarray(a, dtype=np.float64).ravel()
     b = np.asarray(b, dtype=np.float64).ravel()
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300))
+
+
+def exact_apply(Q, K, V, beta, rq=None, rk=None, h=None):
+    """Dense fp64 evaluation of the operator on the fp32 input points."""
+    Q = np.asarray(Q, np.float64)
+    K = np.asarray(K, np.float64)
+    d2 = ((Q[:, None, :] - K[None, :, :]) ** 2).sum(-1)
+    U = np.asarray(V, np.float64).reshape(K.shape[0], -1)
+    if rk is not None:
+        U = U * np.asarray(rk)[:, None]
+    if h is not None:
+        U = U * np.asarray(h)[:, None]
+    out = np.exp(-beta * d2) @ U
+    return out if rq is None else out * np.asarray(rq)[:, None]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -145,9 +162,11 @@ def test_ragged_shapes_vs_oracle(prec, nq, nk, d, r):
     rq, rk, h = rng.uniform(0.5, 2, nq), rng.uniform(0.5, 2, nk), rng.uniform(0.2, 1, nk)
     beta = 1.0 / (2.0 * d)
     ref = O.flash_diffusion(Q, K, V, beta, rq, rk, h)
+    exact = exact_apply(Q, K, V, beta, rq, rk, h)
     out = FlashDiffusion(Q, K, V, beta, rq, rk, h, precision=prec)
     assert out.shape == (nq, r)
-    assert rel_l2(out, ref) <= TOL[prec]
+    assert rel_l2(out, exact) <= TOL[prec]
+    assert rel_l2(out, ref) <= TOL[prec] + rel_l2(ref, exact)
 
 
 def test_empty_key_set_gives_zero():
