@@ -42,6 +42,7 @@ SIGNATURES = {
     "fd_pack_operand": (_I, [_P, _I, _L, _I, _P, _F, _I, _I, _P, _P]),
     "fd_apply_workspace_bytes": (_S, [_L, _L, _I, _I]),
     "fd_apply": (_I, [_P, _L, _P, _L, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P, _S, _P]),
+    "fd_apply_noalloc": (_I, [_P, _L, _P, _L, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "fd_dmap_weights": (_I, [_P, _L, _F, _P, _P]),
     "fd_dmap_rscale": (_I, [_P, _P, _L, _P, _P, _P]),
 }

@@ -144,6 +144,30 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
              const float* row_scale, const float* row_div, void* out, int out_dtype,
              void* workspace, size_t workspace_bytes, void* stream);
 
+/* fd_apply without a workspace argument.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory or cannot pass this library
+ * a device buffer: plugin / FFI hosts with no device allocator to hand over,
+ * processes whose device memory belongs entirely to a fixed pool, and loops
+ * that must avoid the implicit synchronisation of cudaMalloc/cudaFree.  The
+ * scratch lives in one static device array of FD_NOALLOC_SCRATCH_BYTES (8 MiB)
+ * inside the library, held on every GPU that loads the library until the
+ * process exits.  Inputs, operands and the output are still the caller's.
+ *
+ * Limits: 16-bit tiles only (FD_TILE_F16 / FD_TILE_BF16); nk such that
+ * fd_apply_workspace_bytes(nq, nk, r, tile) <= FD_NOALLOC_SCRATCH_BYTES (about
+ * 1.9 million keys on a 148-SM B200), otherwise FD_ERR_WORKSPACE with a message.
+ * The first call on a device looks the array's device address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array, so calls that overlap on the GPU (other
+ * streams, other host threads) race on it; serialise them.  Nothing in the
+ * scratch needs to start at zero.  No allocation of any kind is made. */
+#define FD_NOALLOC_SCRATCH_BYTES (8u << 20)
+int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, int tile,
+                     const void* V, int v_dtype, int r, const float* col_scale, const float* col_h,
+                     const float* row_scale, const float* row_div, void* out, int out_dtype,
+                     void* stream);
+
 /* ---------------------------------------------------------------------------
  * Coifman-Lafon normalisation helpers (FD/dmap.py:108-115,
  * FD/kernel_cuda_sm100.py:89-98), fp32 vectors of length n.
