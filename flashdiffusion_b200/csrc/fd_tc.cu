@@ -6,19 +6,23 @@
 // The packed operands fold the squared norms and -beta*log2(e) into the dot
 // product (layout in fd_common.cuh), so the whole exponent of one (i,j) pair
 // is a single tcgen05 MMA accumulator element; the epilogue is
-// clamp(<=0) -> MUFU ex2 -> FMA with u_j.
+// exp2 (MUFU, or a polynomial on the FMA pipe for a fixed share of the
+// columns) -> packed f32x2 FMA with u_j (staged in shared memory by TMA).
 //
 // CTA = 256 query rows (two 128-row subtiles sharing every key tile) x
 // stream of 128-row key tiles.  Warp roles (18 warps):
 //   warps 0-15  four epilogue warpgroups (subtile s, parity p): WG(s,p) owns the
 //               TMEM S buffer 2s+p and the key tiles of parity p of subtile s
 //   warp  16    TMA producer: query tile once per row tile, key tiles through
-//               a STAGES-deep shared-memory ring (no multicast)
+//               a STAGES-deep shared-memory ring (no multicast), and the
+//               matching 128 values of u through a 4-deep ring (bulk copies)
 //   warp  17    MMA issuer: tcgen05.mma kind::f16, M=128 N=128 K=16 steps
 // Work split: the (row tile, key tile) pairs are cut into gridDim.x contiguous
 // ranges (persistent CTAs, one per SM).  A row tile fully inside one range is
 // written directly; a row tile cut between ranges leaves fp64 partials in the
 // workspace that tc_fixup_kernel sums in CTA order (deterministic).
+#include <cstdlib>
+
 #include "fd_prep.cuh"
 #include "fd_ptx.cuh"
 
@@ -32,12 +36,13 @@ constexpr int BM = 128;     // rows per subtile = TMEM lanes
 constexpr int NSUB = 2;     // subtiles per CTA
 constexpr int ROWS = BM * NSUB;
 constexpr int BN = 128;     // key rows per tile = S columns
-constexpr int NEPI_WARPS = 16;
 constexpr int TMA_WARP = 16;
 constexpr int MMA_WARP = 17;
 constexpr int NTHREADS = 18 * 32;
-constexpr uint32_t BOX_BYTES = 128 * 128;  // one 128-row x 64-col bf16 box (128-byte rows)
+constexpr uint32_t BOX_BYTES = 128 * 128;  // one 128-row x 64-col 16-bit box (128-byte rows)
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int URING = 4;                    // depth of the right-hand-side ring
+constexpr uint32_t U_BYTES = BN * 4;        // one key tile of u (fp32)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per pipeline wait
 
 template <int KB>
@@ -45,9 +50,11 @@ struct Cfg {
     static constexpr int STAGES = KB == 1 ? 6 : (KB == 2 ? 4 : 2);
     static constexpr uint32_t Q_BYTES = NSUB * KB * BOX_BYTES;
     static constexpr uint32_t STAGE_BYTES = KB * BOX_BYTES;
-    static constexpr uint32_t BAR_OFF = Q_BYTES + STAGES * STAGE_BYTES;
-    // barriers: kfull[S], kempty[S], qfull, qempty, sfull[4], sempty[4], rfull[2], rempty[2], done
-    static constexpr int NBARS = 2 * STAGES + 2 + 8 + 4 + 1;
+    static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
+    static constexpr uint32_t BAR_OFF = U_OFF + URING * U_BYTES;
+    // barriers: kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4],
+    //           rfull[2], rempty[2], done
+    static constexpr int NBARS = 2 * STAGES + 2 * URING + 2 + 8 + 4 + 1;
     static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t RED_OFF = (MISC_OFF + 16 + 15) & ~15u;
     static constexpr uint32_t SMEM_BYTES = RED_OFF + NSUB * BM * 8;
@@ -61,11 +68,56 @@ struct Sched {
     __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }
 };
 
-__device__ __forceinline__ bool seg_end(int64_t n, int64_t n1, int64_t n_jt) {
-    return n + 1 == n1 || (n + 1) / n_jt != n / n_jt;
+// ---- exp2 of a pair of exponents --------------------------------------------
+// MUFU: two ex2.approx.ftz.  The exponent is <= 0 up to fp32 rounding of the
+// exactly consistent packed operands, so no clamp at 0 is applied (the
+// reference's clamp of d^2 at 0 only removes rounding noise).
+__device__ __forceinline__ uint64_t exp2_mufu2(uint32_t a, uint32_t b) {
+    return ptx::pack2(ptx::ex2_mufu(__uint_as_float(a)), ptx::ex2_mufu(__uint_as_float(b)));
 }
 
-template <int KB>
+// FMA pipe: 2^x = 2^j 2^f, j = round(x) by the 1.5*2^23 shift, f = x - j in
+// [-1/2, 1/2], 2^f by a degree-4 polynomial (relative error 3.6e-6; fitted by
+// flashdiffusion_b200/csrc/exp2_poly_fit.py), 2^j added into the exponent
+// field with one integer multiply-add.  x is clamped at -125 first so the
+// exponent field cannot underflow.
+__device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {
+    const float x0 = fmaxf(__uint_as_float(a), -125.0f);
+    const float x1 = fmaxf(__uint_as_float(b), -125.0f);
+    const uint64_t X = ptx::pack2(x0, x1);
+    const uint64_t SH = ptx::pack2(12582912.0f, 12582912.0f);
+    const uint64_t T = ptx::add2(X, SH);
+    const uint64_t F = ptx::sub2(X, ptx::sub2(T, SH));
+    uint64_t P = ptx::fma2(ptx::pack2(0.009782912f, 0.009782912f), F, ptx::pack2(0.055976883f, 0.055976883f));
+    P = ptx::fma2(P, F, ptx::pack2(0.2402071f, 0.2402071f));
+    P = ptx::fma2(P, F, ptx::pack2(0.6931136f, 0.6931136f));
+    P = ptx::fma2(P, F, ptx::pack2(1.0f, 1.0f));
+    uint32_t p0, p1, t0, t1;
+    ptx::unpack2(P, p0, p1);
+    ptx::unpack2(T, t0, t1);
+    // the low 9 bits of the shifted value hold j mod 512, so t << 23 == j << 23 (mod 2^32)
+    return ptx::pack2(__uint_as_float(p0 + (t0 << 23)), __uint_as_float(p1 + (t1 << 23)));
+}
+
+// 16 columns of S for r = 1: acc += 2^S . u (column pairs packed).  Columns
+// [0, EMU) of the 16 take the FMA-pipe exponential, the rest MUFU.
+template <int EMU>
+__device__ __forceinline__ void chunk16_r1(const uint32_t (&v)[16], const float* us, uint64_t& acc_a,
+                                           uint64_t& acc_b) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint64_t ua, ub;
+        ptx::lds_pairs(us + 4 * q, ua, ub);
+        const uint64_t e01 = (4 * q + 2 <= EMU) ? exp2_poly2(v[4 * q], v[4 * q + 1])
+                                                : exp2_mufu2(v[4 * q], v[4 * q + 1]);
+        const uint64_t e23 = (4 * q + 4 <= EMU) ? exp2_poly2(v[4 * q + 2], v[4 * q + 3])
+                                                : exp2_mufu2(v[4 * q + 2], v[4 * q + 3]);
+        acc_a = ptx::fma2(e01, ua, acc_a);
+        acc_b = ptx::fma2(e23, ub, acc_b);
+    }
+}
+
+template <int KB, int EMU>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
           const float* __restrict__ u, int64_t nq, int kd, uint32_t idesc, Sched sc, RowEpilogue ep,
@@ -75,10 +127,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = base;
     uint8_t* sK = base + C::Q_BYTES;
+    float* sU = (float*)(base + C::U_OFF);
     uint64_t* bars = (uint64_t*)(base + C::BAR_OFF);
     uint64_t* kfull = bars;
-    uint64_t* kempty = bars + C::STAGES;
-    uint64_t* qfull = bars + 2 * C::STAGES;
+    uint64_t* kempty = kfull + C::STAGES;
+    uint64_t* ufull = kempty + C::STAGES;
+    uint64_t* uempty = ufull + URING;
+    uint64_t* qfull = uempty + URING;
     uint64_t* qempty = qfull + 1;
     uint64_t* sfull = qfull + 2;
     uint64_t* sempty = sfull + 4;
@@ -100,6 +155,10 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
         for (int i = 0; i < C::STAGES; ++i) {
             ptx::mbar_init(&kfull[i], 1);
             ptx::mbar_init(&kempty[i], 1);
+        }
+        for (int i = 0; i < URING; ++i) {
+            ptx::mbar_init(&ufull[i], 1);
+            ptx::mbar_init(&uempty[i], 8);  // the 8 epilogue warps of one parity
         }
         ptx::mbar_init(qfull, 1);
         ptx::mbar_init(qempty, 1);
@@ -133,8 +192,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            for (int64_t n = n0; n < n1; ++n) {
-                const int64_t rt = n / n_jt, jt = n - rt * n_jt;
+            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+                const int64_t m = n - n0;
                 if (rt != cur_rt) {
                     if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
@@ -151,6 +211,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     ptx::tma_load_2d(sK + (stage * KB + kb) * BOX_BYTES, &tmk, &kfull[stage], kb * 64,
                                      (int)(jt * BN));
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                // right-hand side of this key tile into the u ring
+                const int us = (int)(m & (URING - 1));
+                const uint32_t uph = (uint32_t)((m / URING) & 1);
+                if (!ptx::wait_bounded(&uempty[us], uph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                ptx::mbar_expect_tx(&ufull[us], U_BYTES);
+                ptx::bulk_load(sU + us * BN, u + jt * BN, U_BYTES, &ufull[us]);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -159,11 +225,11 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            for (int64_t n = n0; n < n1; ++n) {
+            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
                 const int64_t m = n - n0;
                 const int p = (int)(m & 1);
                 const uint32_t use = (uint32_t)(m >> 1);
-                const int64_t rt = n / n_jt;
                 if (rt != cur_rt) {
                     if (!ptx::wait_bounded(qfull, qcount & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
                     ++qcount;
@@ -186,7 +252,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 }
                 if (!ok) break;
                 ptx::umma_commit(&kempty[stage]);
-                if (seg_end(n, n1, n_jt)) ptx::umma_commit(qempty);
+                if (n + 1 == n1 || jt + 1 == n_jt) ptx::umma_commit(qempty);
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
             // every MMA issued above has completed once `done` flips
@@ -204,36 +270,45 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
         double acc = 0.0;
         uint32_t segs = 0;
         bool alive = true;
-        for (int64_t n = n0; n < n1 && alive; ++n) {
+        int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
+        for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
             const int64_t m = n - n0;
-            const int64_t rt = n / n_jt, jt = n - rt * n_jt;
             if ((int)(m & 1) == p) {
                 const uint32_t use = (uint32_t)(m >> 1);
                 const int b = s * 2 + p;
+                const int us = (int)(m & (URING - 1));
+                if (!ptx::wait_bounded(&ufull[us], (uint32_t)((m / URING) & 1), abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
                 if (!ptx::wait_bounded(&sfull[b], use & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
-                const float4* u4 = (const float4*)(u + jt * BN);
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                const float* ut = sU + us * BN;
+                uint64_t acc_a = 0, acc_b = 0;   // +0.0f pairs
+                // 16-column TMEM loads, double buffered: the load of the next
+                // 16 columns is in flight while the current 16 are computed
+                uint32_t va[16], vb[16];
+                const uint32_t tb = t_lane + b * BN;
+                ptx::tmem_ld16(tb, va);
+                ptx::tmem_wait_ld16(va);
 #pragma unroll 1
-                for (int ch = 0; ch < BN / 32; ++ch) {
-                    uint32_t v[32];
-                    ptx::tmem_ld32(t_lane + b * BN + ch * 32, v);
-                    ptx::tmem_wait_ld(v);
-#pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        const float4 uu = __ldg(u4 + ch * 8 + g);
-                        a0 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 0]), 0.f)), uu.x, a0);
-                        a1 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 1]), 0.f)), uu.y, a1);
-                        a2 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 2]), 0.f)), uu.z, a2);
-                        a3 = fmaf(ptx::ex2_mufu(fminf(__uint_as_float(v[4 * g + 3]), 0.f)), uu.w, a3);
-                    }
+                for (int c = 0; c < BN / 16; c += 2) {
+                    ptx::tmem_ld16(tb + (c + 1) * 16, vb);
+                    chunk16_r1<EMU>(va, ut + c * 16, acc_a, acc_b);
+                    ptx::tmem_wait_ld16(vb);
+                    if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                    chunk16_r1<EMU>(vb, ut + (c + 1) * 16, acc_a, acc_b);
+                    if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
                 }
-                acc += (double)((a0 + a1) + (a2 + a3));
                 ptx::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&sempty[b]);
+                if (lane == 0) {
+                    ptx::mbar_arrive(&sempty[b]);
+                    ptx::mbar_arrive(&uempty[us]);
+                }
+                uint32_t a0, a1, b0, b1;
+                ptx::unpack2(acc_a, a0, a1);
+                ptx::unpack2(acc_b, b0, b1);
+                acc += (double)((__uint_as_float(a0) + __uint_as_float(a1)) + (__uint_as_float(b0) + __uint_as_float(b1)));
             }
-            if (seg_end(n, n1, n_jt)) {
+            if (n + 1 == n1 || jt + 1 == n_jt) {
                 // combine the two parity halves of this subtile, then store
                 const uint32_t ph = segs & 1;
                 if (p == 1) {
@@ -343,15 +418,38 @@ size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
     return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS);
 }
 
-template <int KB>
+template <int KB, int EMU>
 static int launch_tc_kb(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
                         uint32_t idesc, const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
     using C = tc::Cfg<KB>;
-    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
-    tc::tc_kernel<KB><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part);
+    tc::tc_kernel<KB, EMU><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
+}
+
+// Columns per 16 whose exp2 runs on the FMA pipe instead of MUFU.  Default 0;
+// FD_EXP2_FMA_COLS (0, 2, 4 or 6) overrides it for tuning.
+static int exp2_fma_cols() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("FD_EXP2_FMA_COLS");
+        const int x = e ? atoi(e) : 0;
+        v = (x == 0 || x == 2 || x == 4 || x == 6) ? x : 0;
+    }
+    return v;
+}
+
+template <int KB>
+static int launch_tc_emu(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
+                         uint32_t idesc, const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
+    switch (exp2_fma_cols()) {
+        case 2: return launch_tc_kb<KB, 2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
+        case 4: return launch_tc_kb<KB, 4>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
+        case 6: return launch_tc_kb<KB, 6>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
+        default: return launch_tc_kb<KB, 0>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
+    }
 }
 
 int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
@@ -376,9 +474,9 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     double* part = (double*)ws;
     const float* u = (const float*)rhs;
     switch (kb) {
-        case 1: FD_TRY(launch_tc_kb<1>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
-        case 2: FD_TRY(launch_tc_kb<2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
-        default: FD_TRY(launch_tc_kb<3>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+        case 1: FD_TRY(launch_tc_emu<1>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+        case 2: FD_TRY(launch_tc_emu<2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+        default: FD_TRY(launch_tc_emu<3>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
     }
     tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(part, sc, nq, ep);
     FD_CUDA_TRY(cudaGetLastError());
