@@ -35,16 +35,26 @@ static bool valid_dtype(int t) { return t == FD_DTYPE_F32 || t == FD_DTYPE_F16 |
 static bool valid_tile(int t) { return t == FD_TILE_BF16 || t == FD_TILE_F32 || t == FD_TILE_F16; }
 
 // columns of V handled per tile-kernel launch
-static int cols_per_launch(int tile) { return tile == FD_TILE_F32 ? 64 : 1; }
+static int cols_per_launch(int tile, int r) {
+    if (tile == FD_TILE_F32) return 64;
+    return r == 1 ? 1 : 64;
+}
 
+// prepared right-hand side: fp32 u (r = 1 tensor-core and fp32 paths) or the
+// transposed, column-scaled fp16 block plus 2 x 64 column words (block path)
 static size_t rhs_bytes(int64_t nk, int r, int tile) {
-    const int rc = std::min(r, cols_per_launch(tile));
-    return align256(sizeof(float) * (size_t)round_up(std::max<int64_t>(nk, 1), 128) * rc);
+    const int rc = std::min(r, cols_per_launch(tile, r));
+    const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
+    if (is_tc_tile(tile) && r > 1)
+        return align256(sizeof(__half) * 2 * (size_t)nk_pad * block_rp(rc)) + align256(sizeof(float) * 128);
+    return align256(sizeof(float) * (size_t)nk_pad * rc);
 }
 
 static size_t kernel_ws_bytes(int64_t nq, int64_t nk, int r, int tile) {
-    const int rc = std::min(r, cols_per_launch(tile));
-    return tile == FD_TILE_F32 ? simt_workspace_bytes(nq, nk, rc) : tc_workspace_bytes(nq, nk, rc);
+    const int rc = std::min(r, cols_per_launch(tile, r));
+    if (tile == FD_TILE_F32) return simt_workspace_bytes(nq, nk, rc);
+    if (r > 1) return tc_block_workspace_bytes(block_rp(rc));
+    return tc_workspace_bytes(nq, nk, rc);
 }
 
 }  // namespace fd
@@ -127,7 +137,7 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
                  "workspace must be non-null and 256-byte aligned");
     if (nq == 0) return FD_OK;
 
-    const int cpl = cols_per_launch(tile);
+    const int cpl = cols_per_launch(tile, r);
     const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
     uint8_t* ws = (uint8_t*)workspace;
     float* u = (float*)ws;
@@ -137,6 +147,15 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
         const int rc = std::min(cpl, r - c0);
         RowEpilogue ep{row_scale, row_div, out, out_dtype, (int64_t)r, c0};
         if (nk == 0) { FD_TRY(launch_zero_rows(nq, rc, ep, s)); continue; }
+        if (is_tc_tile(tile) && r > 1) {
+            const int rp = block_rp(rc);
+            __half* ut = (__half*)ws;
+            float* colscale = (float*)(ws + align256(sizeof(__half) * 2 * (size_t)nk_pad * rp));
+            unsigned* colmax = (unsigned*)(colscale + 64);
+            FD_TRY(launch_rhs_f16t(V, v_dtype, nk, nk_pad, r, c0, rc, rp, col_scale, col_h, colmax, ut, colscale, s));
+            FD_TRY(launch_tc_block(Qop, nq, Kop, nk, d, tile, ut, nk_pad, colscale, rc, ep, kws, kws_bytes, s));
+            continue;
+        }
         FD_TRY(launch_rhs_f32(V, v_dtype, nk, nk_pad, r, c0, rc, col_scale, col_h, u, s));
         if (tile == FD_TILE_F32) {
             const float* qp = (const float*)Qop;

@@ -156,6 +156,64 @@ __global__ void rhs_bf16t_kernel(const void* __restrict__ V, int v_dtype, int64_
     }
 }
 
+// Per-column maximum of |col_scale_j col_h_j V[j*ldv + c0 + c]| over j, as the
+// bit pattern of a non-negative float (so integer atomicMax orders it).
+__global__ void rhs_colmax_kernel(const void* __restrict__ V, int v_dtype, int64_t nk, int ldv, int c0, int rc,
+                                  const float* __restrict__ cs, const float* __restrict__ ch,
+                                  unsigned* __restrict__ colmax) {
+    __shared__ unsigned smax[64];
+    for (int c = threadIdx.x; c < rc; c += blockDim.x) smax[c] = 0u;
+    __syncthreads();
+    const int64_t total = nk * rc;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = e / rc;
+        const int c = (int)(e % rc);
+        double x = V ? load_as_f64(V, v_dtype, j * ldv + c0 + c) : 1.0;
+        if (cs) x *= (double)cs[j];
+        if (ch) x *= (double)ch[j];
+        atomicMax(&smax[c], __float_as_uint(fabsf((float)x)));
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < rc; c += blockDim.x) atomicMax(&colmax[c], smax[c]);
+}
+
+// Transposed fp16 hi/lo right-hand side with a power-of-two scale per column:
+// with x = u_jc / 2^k_c, ut[c*ld + j] = fp16(x) and ut[(rp + c)*ld + j] =
+// fp16(x - fp16(x)); colscale[c] = 2^k_c with max_j |u_jc| / 2^k_c in [1/2, 1).
+// Rows rc..rp-1 (of both halves) and columns nk..ld-1 are zero.
+__global__ void rhs_f16t_kernel(const void* __restrict__ V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0,
+                                int rc, int rp, const float* __restrict__ cs, const float* __restrict__ ch,
+                                const unsigned* __restrict__ colmax, __half* __restrict__ ut,
+                                float* __restrict__ colscale) {
+    if (blockIdx.x == 0)
+        for (int c = threadIdx.x; c < rp; c += blockDim.x) {
+            int k = 0;
+            const float m = c < rc ? __uint_as_float(colmax[c]) : 0.f;
+            if (m > 0.f) frexpf(m, &k);
+            colscale[c] = ldexpf(1.0f, k);
+        }
+    const int64_t total = ld * rp;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int c = (int)(e / ld);
+        const int64_t j = e - (int64_t)c * ld;
+        float val = 0.f;
+        if (c < rc && j < nk) {
+            double x = V ? load_as_f64(V, v_dtype, j * ldv + c0 + c) : 1.0;
+            if (cs) x *= (double)cs[j];
+            if (ch) x *= (double)ch[j];
+            int k = 0;
+            const float m = __uint_as_float(colmax[c]);
+            if (m > 0.f) frexpf(m, &k);
+            val = (float)ldexp(x, -k);
+        }
+        const __half hi = __float2half_rn(val);
+        ut[e] = hi;
+        ut[e + ld * rp] = __float2half_rn(val - __half2float(hi));
+    }
+}
+
 __global__ void dmap_weights_kernel(const float* __restrict__ D, int64_t n, float alpha,
                                     float* __restrict__ w) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -237,6 +295,20 @@ int launch_rhs_bf16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv
     if (total == 0) return FD_OK;
     const int grid = (int)std::min<int64_t>(cdiv(total, 256), 148 * 16);
     rhs_bf16t_kernel<<<grid, 256, 0, s>>>(V, v_dtype, nk, ld, ldv, c0, rc, cs, ch, ut);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+int launch_rhs_f16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0, int rc, int rp,
+                    const float* cs, const float* ch, unsigned* colmax, __half* ut, float* colscale, cudaStream_t s) {
+    FD_CUDA_TRY(cudaMemsetAsync(colmax, 0, sizeof(unsigned) * rp, s));
+    if (nk > 0) {
+        const int g1 = (int)std::min<int64_t>(cdiv(nk * rc, 256), 148 * 4);
+        rhs_colmax_kernel<<<g1, 256, 0, s>>>(V, v_dtype, nk, ldv, c0, rc, cs, ch, colmax);
+        FD_CUDA_TRY(cudaGetLastError());
+    }
+    const int g2 = (int)std::min<int64_t>(cdiv(ld * rp, 256), 148 * 16);
+    rhs_f16t_kernel<<<g2, 256, 0, s>>>(V, v_dtype, nk, ld, ldv, c0, rc, rp, cs, ch, colmax, ut, colscale);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }

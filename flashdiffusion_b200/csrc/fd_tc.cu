@@ -23,8 +23,7 @@
 // workspace that tc_fixup_kernel sums in CTA order (deterministic).
 #include <cstdlib>
 
-#include "fd_prep.cuh"
-#include "fd_ptx.cuh"
+#include "fd_tc_common.cuh"
 
 namespace fd {
 
@@ -61,44 +60,6 @@ struct Cfg {
     static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for 1024-byte alignment
 };
 
-struct Sched {
-    int64_t n_jt;    // key tiles per row tile
-    int64_t units;   // n_rt * n_jt
-    int grid;
-    __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }
-};
-
-// ---- exp2 of a pair of exponents --------------------------------------------
-// MUFU: two ex2.approx.ftz.  The exponent is <= 0 up to fp32 rounding of the
-// exactly consistent packed operands, so no clamp at 0 is applied (the
-// reference's clamp of d^2 at 0 only removes rounding noise).
-__device__ __forceinline__ uint64_t exp2_mufu2(uint32_t a, uint32_t b) {
-    return ptx::pack2(ptx::ex2_mufu(__uint_as_float(a)), ptx::ex2_mufu(__uint_as_float(b)));
-}
-
-// FMA pipe: 2^x = 2^j 2^f, j = round(x) by the 1.5*2^23 shift, f = x - j in
-// [-1/2, 1/2], 2^f by a degree-4 polynomial (relative error 3.6e-6; fitted by
-// flashdiffusion_b200/csrc/exp2_poly_fit.py), 2^j added into the exponent
-// field with one integer multiply-add.  x is clamped at -125 first so the
-// exponent field cannot underflow.
-__device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {
-    const float x0 = fmaxf(__uint_as_float(a), -125.0f);
-    const float x1 = fmaxf(__uint_as_float(b), -125.0f);
-    const uint64_t X = ptx::pack2(x0, x1);
-    const uint64_t SH = ptx::pack2(12582912.0f, 12582912.0f);
-    const uint64_t T = ptx::add2(X, SH);
-    const uint64_t F = ptx::sub2(X, ptx::sub2(T, SH));
-    uint64_t P = ptx::fma2(ptx::pack2(0.009782912f, 0.009782912f), F, ptx::pack2(0.055976883f, 0.055976883f));
-    P = ptx::fma2(P, F, ptx::pack2(0.2402071f, 0.2402071f));
-    P = ptx::fma2(P, F, ptx::pack2(0.6931136f, 0.6931136f));
-    P = ptx::fma2(P, F, ptx::pack2(1.0f, 1.0f));
-    uint32_t p0, p1, t0, t1;
-    ptx::unpack2(P, p0, p1);
-    ptx::unpack2(T, t0, t1);
-    // the low 9 bits of the shifted value hold j mod 512, so t << 23 == j << 23 (mod 2^32)
-    return ptx::pack2(__uint_as_float(p0 + (t0 << 23)), __uint_as_float(p1 + (t1 << 23)));
-}
-
 // 16 columns of S for r = 1: acc += 2^S . u (column pairs packed).  Columns
 // [0, EMU) of the 16 take the FMA-pipe exponential, the rest MUFU.
 template <int EMU>
@@ -121,7 +82,7 @@ template <int KB, int EMU>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
           const float* __restrict__ u, int64_t nq, int kd, uint32_t idesc, Sched sc, RowEpilogue ep,
-          double* __restrict__ part) {
+          double* __restrict__ part, int* __restrict__ status) {
     using C = Cfg<KB>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -196,7 +157,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
                 const int64_t m = n - n0;
                 if (rt != cur_rt) {
-                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
                     for (int s = 0; s < NSUB; ++s)
                         for (int kb = 0; kb < KB; ++kb)
@@ -205,7 +166,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     cur_rt = rt;
                     ++qcount;
                 }
-                if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
                 for (int kb = 0; kb < KB; ++kb)
                     ptx::tma_load_2d(sK + (stage * KB + kb) * BOX_BYTES, &tmk, &kfull[stage], kb * 64,
@@ -214,7 +175,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 // right-hand side of this key tile into the u ring
                 const int us = (int)(m & (URING - 1));
                 const uint32_t uph = (uint32_t)((m / URING) & 1);
-                if (!ptx::wait_bounded(&uempty[us], uph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                if (!ptx::wait_bounded(&uempty[us], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&ufull[us], U_BYTES);
                 ptx::bulk_load(sU + us * BN, u + jt * BN, U_BYTES, &ufull[us]);
             }
@@ -231,15 +192,15 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 const int p = (int)(m & 1);
                 const uint32_t use = (uint32_t)(m >> 1);
                 if (rt != cur_rt) {
-                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ++qcount;
                     cur_rt = rt;
                 }
-                if (!ptx::wait_bounded(&kfull[stage], kph, abort, &g_fd_status, WAIT_LIMIT_NS)) break;
+                if (!ptx::wait_bounded(&kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
                 bool ok = true;
                 for (int s = 0; s < NSUB && ok; ++s) {
                     const int b = s * 2 + p;
-                    if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
                     ptx::tc_fence_after();
                     const uint32_t qa = q_base + s * KB * BOX_BYTES;
                     const uint32_t ka = k_base + stage * C::STAGE_BYTES;
@@ -257,7 +218,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             }
             // every MMA issued above has completed once `done` flips
             ptx::umma_commit(done);
-            ptx::wait_bounded(done, 0, abort, &g_fd_status, WAIT_LIMIT_NS);
+            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
         }
     } else {
         // ---- epilogue warpgroups ------------------------------------------
@@ -277,8 +238,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 const uint32_t use = (uint32_t)(m >> 1);
                 const int b = s * 2 + p;
                 const int us = (int)(m & (URING - 1));
-                if (!ptx::wait_bounded(&ufull[us], (uint32_t)((m / URING) & 1), abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
-                if (!ptx::wait_bounded(&sfull[b], use & 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                if (!ptx::wait_bounded(&ufull[us], (uint32_t)((m / URING) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                if (!ptx::wait_bounded(&sfull[b], use & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
                 const float* ut = sU + us * BN;
                 uint64_t acc_a = 0, acc_b = 0;   // +0.0f pairs
@@ -312,11 +273,11 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 // combine the two parity halves of this subtile, then store
                 const uint32_t ph = segs & 1;
                 if (p == 1) {
-                    if (!ptx::wait_bounded(&rempty[s], ph ^ 1, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    if (!ptx::wait_bounded(&rempty[s], ph ^ 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                     red[s * BM + quarter * 32 + lane] = acc;
                     ptx::mbar_arrive(&rfull[s]);
                 } else {
-                    if (!ptx::wait_bounded(&rfull[s], ph, abort, &g_fd_status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    if (!ptx::wait_bounded(&rfull[s], ph, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                     const double tot = acc + red[s * BM + quarter * 32 + lane];
                     ptx::mbar_arrive(&rempty[s]);
                     const int64_t gi = rt * ROWS + row_in_tile;
@@ -391,7 +352,7 @@ static int get_encode(EncodeTiledFn* fn) {
 }
 
 // 2-D bf16 map over a [rows][cols] row-major matrix, 64 x box_rows boxes, 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16) {
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16) {
     EncodeTiledFn enc;
     FD_TRY(get_encode(&enc));
     FD_CHECK_ARG(((uintptr_t)ptr & 15) == 0, "tile operand must be 16-byte aligned");
@@ -407,7 +368,7 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
     return FD_OK;
 }
 
-static int num_sms() {
+int num_sms() {
     int dev = 0, n = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     return n;
@@ -424,7 +385,10 @@ static int launch_tc_kb(const CUtensorMap& mq, const CUtensorMap& mk, const floa
     using C = tc::Cfg<KB>;
     FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
-    tc::tc_kernel<KB, EMU><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part);
+    int* status = nullptr;
+    FD_TRY(status_word(&status));
+    tc::tc_kernel<KB, EMU><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part,
+                                                                        status);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
@@ -464,8 +428,8 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "16-bit tile path: workspace %zu B < %zu B", ws_bytes, need);
     CUtensorMap mq, mk;
     const bool f16 = tile == FD_TILE_F16;
-    FD_TRY(make_map(&mq, qop, nq, kd, tc::BM, f16));
-    FD_TRY(make_map(&mk, kop, nk, kd, tc::BN, f16));
+    FD_TRY(make_tile_map(&mq, qop, nq, kd, tc::BM, f16));
+    FD_TRY(make_tile_map(&mk, kop, nk, kd, tc::BN, f16));
     const uint32_t idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
     tc::Sched sc;
     sc.n_jt = cdiv(nk, tc::BN);

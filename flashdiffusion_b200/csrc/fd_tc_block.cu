@@ -1,0 +1,456 @@
+// Block right-hand sides (r > 1) on the 16-bit tensor-core path: two tcgen05
+// GEMMs per key tile.
+//
+//   S = Q~ K~^T            (tcgen05.mma, A and B from shared memory, fp32 in TMEM)
+//   P = 2^S                (epilogue warps: MUFU ex2, split P = P_hi + P_lo into two
+//                           fp16 parts written back to TMEM over S columns each
+//                           warpgroup has already read)
+//   O += P_hi U_hi + P_hi U_lo + P_lo U_hi
+//                          (three tcgen05.mma per 16 keys, A from TMEM, B = U^T
+//                           tiles in shared memory): fp32-class products from
+//                           fp16 operands, so the block path keeps the accuracy
+//                           of the r = 1 path (which multiplies in fp32)
+//
+// U = diag(col_scale * col_h) V, stored transposed as fp16 hi/lo pairs with one
+// power-of-two scale per column (so every column uses the fp16 range; the
+// scale is undone in the output epilogue).  There is no online softmax: the row scale is a
+// known vector, applied once per output row.
+//
+// CTA = 128 query rows x stream of 128-key tiles.  Warp roles (18 warps):
+//   warps 0-15  four epilogue warpgroups WG(p, h): parity p of the key tile
+//               (TMEM S/P buffer p) and column half h of it
+//   warp  16    TMA producer: query tile per row tile; per key tile the K
+//               box(es) and the 64-key boxes of U_hi^T and U_lo^T (no multicast)
+//   warp  17    MMA issuer: Q.K^T of tile m, then P.U of tile m-1 (so the
+//               tensor pipe never waits for one epilogue), all P.U products
+//               of a row tile accumulating into ONE TMEM accumulator O
+// The persistent work split and the deterministic cross-CTA fix-up are the
+// ones of the r = 1 kernel (fd_tc.cu).
+#include "fd_tc_common.cuh"
+
+namespace fd {
+namespace tcb {
+
+using tc::Sched;
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int TMA_WARP = 16;
+constexpr int MMA_WARP = 17;
+constexpr int NTHREADS = 18 * 32;
+constexpr uint32_t BOX_BYTES = 128 * 128;  // 128 rows x 64 16-bit columns
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 256;            // O accumulator columns [256, 256 + RP)
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+template <int KB, int RP>
+struct Cfg {
+    static constexpr uint32_t Q_BYTES = KB * BOX_BYTES;
+    static constexpr uint32_t UT_BOX = RP * 128;                 // RP rows x 64 keys
+    static constexpr uint32_t STAGE_BYTES = KB * BOX_BYTES + 4 * UT_BOX;   // K, U_hi^T (2 boxes), U_lo^T (2)
+    static constexpr int STAGES_RAW = (int)((222u * 1024u - Q_BYTES) / STAGE_BYTES);
+    static constexpr int STAGES = STAGES_RAW > 6 ? 6 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
+    static constexpr uint32_t BAR_OFF = Q_BYTES + STAGES * STAGE_BYTES;
+    // kfull[S], kempty[S], qfull, qempty, sfull[2], sempty[2], pfull[2], ofull, oempty, done
+    static constexpr int NBARS = 2 * STAGES + 2 + 6 + 3;
+    static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
+    static constexpr uint32_t SMEM_BYTES = MISC_OFF + 16;
+    static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
+    static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
+};
+
+// Load `RP / 4` consecutive O columns of this thread's row.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&o)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, float (&o)[16]) {
+    uint32_t v[16];
+    ptx::tmem_ld16(taddr, v);
+    ptx::tmem_wait_ld16(v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(v[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<8>(uint32_t taddr, float (&o)[8]) {
+    uint32_t v[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7])
+                 :: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(v[i]);
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cols<4>(uint32_t taddr, float (&o)[4]) {
+    uint32_t v[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]) :: "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __uint_as_float(v[i]);
+}
+
+// 32 lanes x 8 columns <- 8 registers (16 fp16 values of P per thread).
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// 16 S values -> P = 2^S as fp16 hi and lo parts (P - hi, exact in fp32 before
+// rounding), each packed in 8 registers with key 2c in the low half.
+__device__ __forceinline__ void exp2_to_f16x2(const uint32_t (&v)[16], uint32_t (&hi)[8], uint32_t (&lo)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float e0 = ptx::ex2_mufu(__uint_as_float(v[2 * i]));
+        const float e1 = ptx::ex2_mufu(__uint_as_float(v[2 * i + 1]));
+        const __half2 h = __floats2half2_rn(e0, e1);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn(e0 - hf.x, e1 - hf.y);
+        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+}
+
+template <int KB, int RP>
+__global__ void __launch_bounds__(NTHREADS, 1)
+tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
+                int64_t nq, int kd, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
+                double* __restrict__ part, int* __restrict__ status) {
+    using C = Cfg<KB, RP>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = base;
+    uint8_t* sK = base + C::Q_BYTES;
+    uint64_t* bars = (uint64_t*)(base + C::BAR_OFF);
+    uint64_t* kfull = bars;
+    uint64_t* kempty = kfull + C::STAGES;
+    uint64_t* qfull = kempty + C::STAGES;
+    uint64_t* qempty = qfull + 1;
+    uint64_t* sfull = qfull + 2;
+    uint64_t* sempty = sfull + 2;
+    uint64_t* pfull = sempty + 2;
+    uint64_t* ofull = pfull + 2;
+    uint64_t* oempty = ofull + 1;
+    uint64_t* done = oempty + 1;
+    uint32_t* tmem_slot = (uint32_t*)(base + C::MISC_OFF);
+    volatile int* abort = (volatile int*)(base + C::MISC_OFF + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+    const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
+    const int64_t n_jt = sc.n_jt;
+    const int ksteps = kd / 16;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::STAGES; ++i) {
+            ptx::mbar_init(&kfull[i], 1);
+            ptx::mbar_init(&kempty[i], 1);
+        }
+        ptx::mbar_init(qfull, 1);
+        ptx::mbar_init(qempty, 1);
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(&sfull[i], 1);
+            ptx::mbar_init(&sempty[i], 1);
+            ptx::mbar_init(&pfull[i], 8);   // the 8 epilogue warps of one parity
+        }
+        ptx::mbar_init(ofull, 1);
+        ptx::mbar_init(oempty, 16);         // every epilogue warp reads its share of O
+        ptx::mbar_init(done, 1);
+        *abort = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == MMA_WARP) {
+        ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    if (warp == TMA_WARP && lane == 0) {
+        ptx::prefetch_tmap(&tmq);
+        ptx::prefetch_tmap(&tmk);
+        ptx::prefetch_tmap(&tmu);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == TMA_WARP) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t kph = 0, qcount = 0;
+            int64_t cur_rt = -1;
+            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+                if (rt != cur_rt) {
+                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    ptx::mbar_expect_tx(qfull, C::Q_BYTES);
+                    for (int kb = 0; kb < KB; ++kb)
+                        ptx::tma_load_2d(sQ + kb * BOX_BYTES, &tmq, qfull, kb * 64, (int)(rt * BM));
+                    cur_rt = rt;
+                    ++qcount;
+                }
+                if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                uint8_t* st = sK + stage * C::STAGE_BYTES;
+                ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
+                for (int kb = 0; kb < KB; ++kb)
+                    ptx::tma_load_2d(st + kb * BOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
+                for (int part2 = 0; part2 < 2; ++part2)
+                    for (int h = 0; h < 2; ++h)
+                        ptx::tma_load_2d(st + KB * BOX_BYTES + (part2 * 2 + h) * C::UT_BOX, &tmu, &kfull[stage],
+                                         (int)(jt * BN + h * 64), part2 * RP);
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+        }
+    } else if (warp == MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
+            int stage = 0;
+            uint32_t kph = 0, qcount = 0, ocount = 0;
+            int64_t cur_rt = -1;
+            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            // the P.U product of the previous tile, issued after the next Q.K^T
+            bool have_pend = false, pend_last = false, fresh = true;
+            int pend_stage = 0;
+            int64_t pend_m = 0;
+            auto issue_pv = [&]() -> bool {
+                const int pb = (int)(pend_m & 1);
+                if (!ptx::wait_bounded(&pfull[pb], (uint32_t)((pend_m >> 1) & 1), abort, status, WAIT_LIMIT_NS)) return false;
+                if (fresh && !ptx::wait_bounded(oempty, (ocount & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) return false;
+                ptx::tc_fence_after();
+                const uint32_t ut = k_base + pend_stage * C::STAGE_BYTES + KB * BOX_BYTES;
+#pragma unroll 1
+                for (int ks = 0; ks < BN / 16; ++ks) {
+                    const uint32_t off = (ks >> 2) * C::UT_BOX + (ks & 3) * 32;
+                    const uint64_t uhi = ptx::sw128_kmajor_desc(ut + off);
+                    const uint64_t ulo = ptx::sw128_kmajor_desc(ut + 2 * C::UT_BOX + off);
+                    // keys 16ks..16ks+15: P_hi in 8 columns, P_lo in the next 8
+                    const uint32_t ahi = tmem + pb * BN + ks * 16;
+                    ptx::umma_ts(tmem + O_COL, ahi, uhi, idesc_pv, (fresh && ks == 0) ? 0u : 1u);
+                    ptx::umma_ts(tmem + O_COL, ahi, ulo, idesc_pv, 1u);
+                    ptx::umma_ts(tmem + O_COL, ahi + 8, uhi, idesc_pv, 1u);
+                }
+                fresh = false;
+                ptx::umma_commit(&sempty[pb]);
+                ptx::umma_commit(&kempty[pend_stage]);
+                if (pend_last) {
+                    ptx::umma_commit(ofull);
+                    fresh = true;
+                    ++ocount;
+                }
+                return true;
+            };
+            bool ok = true;
+            for (int64_t n = n0; n < n1 && ok; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+                const int64_t m = n - n0;
+                const int b = (int)(m & 1);
+                if (rt != cur_rt) {
+                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    ++qcount;
+                    cur_rt = rt;
+                }
+                if (!ptx::wait_bounded(&kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
+                if (!ptx::wait_bounded(&sempty[b], (uint32_t)(((m >> 1) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
+                ptx::tc_fence_after();
+                const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                    ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + off),
+                                 ptx::sw128_kmajor_desc(ka + off), idesc_qk, ks > 0);
+                }
+                ptx::umma_commit(&sfull[b]);
+                const bool last = (n + 1 == n1) || (jt + 1 == n_jt);
+                if (last) ptx::umma_commit(qempty);
+                if (have_pend) ok = issue_pv();
+                have_pend = true;
+                pend_m = m;
+                pend_stage = stage;
+                pend_last = last;
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+            if (ok && have_pend) issue_pv();
+            ptx::umma_commit(done);
+            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
+        }
+    } else {
+        // ---- epilogue warpgroups ------------------------------------------
+        const int wg = warp >> 2;
+        const int p = wg & 1, h = wg >> 1;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        const int64_t first_rt = n0 / n_jt;
+        uint32_t segs = 0;
+        bool alive = true;
+        int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
+        for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+            const int64_t m = n - n0;
+            if ((int)(m & 1) == p) {
+                if (!ptx::wait_bounded(&sfull[p], (uint32_t)((m >> 1) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ptx::tc_fence_after();
+                // S columns of this half; the 16 keys of chunk c come back as
+                // P_hi (8 columns) and P_lo (8 columns) over the same 16 S
+                // columns, which this thread has read before it writes them
+                const uint32_t tb = t_lane + p * BN + h * 64;
+                uint32_t va[16], vb[16], ph[8], pl[8];
+                ptx::tmem_ld16(tb, va);
+                ptx::tmem_wait_ld16(va);
+#pragma unroll 1
+                for (int c = 0; c < 4; c += 2) {
+                    ptx::tmem_ld16(tb + (c + 1) * 16, vb);
+                    exp2_to_f16x2(va, ph, pl);
+                    tmem_st8(tb + c * 16, ph);
+                    tmem_st8(tb + c * 16 + 8, pl);
+                    ptx::tmem_wait_ld16(vb);
+                    if (c + 2 < 4) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                    exp2_to_f16x2(vb, ph, pl);
+                    tmem_st8(tb + (c + 1) * 16, ph);
+                    tmem_st8(tb + (c + 1) * 16 + 8, pl);
+                    if (c + 2 < 4) ptx::tmem_wait_ld16(va);
+                }
+                ptx::tmem_wait_st();
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&pfull[p]);
+            }
+            if (n + 1 == n1 || jt + 1 == n_jt) {
+                // read this warpgroup's quarter of the O columns, scale, store
+                if (!ptx::wait_bounded(ofull, segs & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ptx::tc_fence_after();
+                constexpr int NC = RP / 4;
+                const int c0 = wg * NC;
+                float o[NC];
+                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(oempty);
+                const int64_t gi = rt * BM + row;
+                const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
+                const bool full = seg_first == 0 && jt == n_jt - 1;
+                if (gi < nq) {
+#pragma unroll
+                    for (int i = 0; i < NC; ++i) {
+                        const int c = c0 + i;
+                        if (c >= rc) break;
+                        const double val = (double)o[i] * (double)colscale[c];
+                        if (full) store_out(ep, gi, c, val);
+                        else part[(((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * BM + row) * RP + c] = val;
+                    }
+                }
+                ++segs;
+            }
+        }
+        ptx::tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == MMA_WARP) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Sum the partials of row tiles cut between CTA ranges, in CTA order.
+__global__ void tc_block_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, int rc, int rp,
+                                      RowEpilogue ep) {
+    const int64_t rt = blockIdx.x;
+    const int64_t lo = rt * sc.n_jt, hi = lo + sc.n_jt - 1;
+    auto owner = [&](int64_t n) {
+        int c = (int)(n * sc.grid / sc.units);
+        if (c >= sc.grid) c = sc.grid - 1;
+        while (c + 1 < sc.grid && sc.start(c + 1) <= n) ++c;
+        while (c > 0 && sc.start(c) > n) --c;
+        return c;
+    };
+    const int c_lo = owner(lo), c_hi = owner(hi);
+    if (c_lo == c_hi) return;
+    for (int e = threadIdx.x; e < BM * rc; e += blockDim.x) {
+        const int r = e / rc, col = e % rc;
+        const int64_t gi = rt * BM + r;
+        if (gi >= nq) continue;
+        double sum = 0.0;
+        for (int c = c_lo; c <= c_hi; ++c) {
+            const int64_t st = sc.start(c);
+            if (st == sc.start(c + 1)) continue;
+            const int slot = (st / sc.n_jt == rt) ? 0 : 1;
+            sum += part[(((int64_t)c * 2 + slot) * BM + r) * rp + col];
+        }
+        store_out(ep, gi, col, sum);
+    }
+}
+
+}  // namespace tcb
+
+int block_rp(int rc) { return rc <= 16 ? 16 : (rc <= 32 ? 32 : 64); }
+
+size_t tc_block_workspace_bytes(int rp) {
+    return align256(sizeof(double) * 2 * (size_t)num_sms() * tcb::BM * rp);
+}
+
+template <int KB, int RP>
+static int launch_block_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mu, const float* colscale,
+                          int rc, int64_t nq, int kd, uint32_t iqk, uint32_t ipv, const tc::Sched& sc,
+                          const RowEpilogue& ep, double* part, cudaStream_t s) {
+    using C = tcb::Cfg<KB, RP>;
+    int* status = nullptr;
+    FD_TRY(status_word(&status));
+    FD_CUDA_TRY(cudaFuncSetAttribute(tcb::tc_block_kernel<KB, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)C::SMEM_ALLOC));
+    tcb::tc_block_kernel<KB, RP><<<sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, mu, colscale, rc, nq, kd, iqk,
+                                                                               ipv, sc, ep, part, status);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+template <int KB>
+static int launch_block_kb(int rp, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mu,
+                           const float* colscale, int rc, int64_t nq, int kd, uint32_t iqk, uint32_t ipv,
+                           const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
+    switch (rp) {
+        case 16: return launch_block_t<KB, 16>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
+        case 32: return launch_block_t<KB, 32>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
+        default: return launch_block_t<KB, 64>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
+    }
+}
+
+// ut: [2 rp][ld] fp16 transposed, column-scaled right-hand side (hi rows, then
+// lo rows); colscale: rp floats.
+int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile, const void* ut,
+                    int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes,
+                    cudaStream_t s) {
+    if (nq == 0) return FD_OK;
+    if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
+    FD_CHECK_ARG(rc >= 1 && rc <= 64, "block tile path: %d columns per launch (max 64)", rc);
+    const int rp = block_rp(rc);
+    const int kd = kd_bf16(d);
+    const int kb = (int)cdiv(kd, 64);
+    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path supports d <= 186 (got d=%d)", d);
+    const size_t need = tc_block_workspace_bytes(rp);
+    if (ws_bytes < need)
+        return set_error(FD_ERR_WORKSPACE, "block tile path: workspace %zu B < %zu B", ws_bytes, need);
+    const bool f16 = tile == FD_TILE_F16;
+    CUtensorMap mq, mk, mu;
+    FD_TRY(make_tile_map(&mq, qop, nq, kd, tcb::BM, f16));
+    FD_TRY(make_tile_map(&mk, kop, nk, kd, tcb::BN, f16));
+    FD_TRY(make_tile_map(&mu, ut, 2 * rp, ld, rp, true));   // U_hi^T rows then U_lo^T rows
+    const uint32_t iqk = ptx::idesc_f32acc(tcb::BM, tcb::BN, f16);
+    const uint32_t ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
+    tc::Sched sc;
+    sc.n_jt = cdiv(nk, tcb::BN);
+    sc.units = cdiv(nq, tcb::BM) * sc.n_jt;
+    sc.grid = (int)std::min<int64_t>(num_sms(), sc.units);
+    double* part = (double*)ws;
+    switch (kb) {
+        case 1: FD_TRY(launch_block_kb<1>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
+        case 2: FD_TRY(launch_block_kb<2>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
+        default: FD_TRY(launch_block_kb<3>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
+    }
+    tcb::tc_block_fixup_kernel<<<(unsigned)cdiv(nq, tcb::BM), 256, 0, s>>>(part, sc, nq, rc, rp, ep);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+}  // namespace fd

@@ -1,0 +1,54 @@
+// Pieces shared by the tcgen05 tile kernels (fd_tc.cu: r = 1, fd_tc_block.cu:
+// block right-hand sides): the persistent work split and the two exp2 paths.
+#pragma once
+#include "fd_prep.cuh"
+#include "fd_ptx.cuh"
+
+namespace fd {
+namespace tc {
+
+struct Sched {
+    int64_t n_jt;    // key tiles per row tile
+    int64_t units;   // n_rt * n_jt
+    int grid;
+    __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }
+};
+
+// ---- exp2 of a pair of exponents --------------------------------------------
+// MUFU: two ex2.approx.ftz.  The exponent is <= 0 up to fp32 rounding of the
+// exactly consistent packed operands, so no clamp at 0 is applied (the
+// reference's clamp of d^2 at 0 only removes rounding noise).
+__device__ __forceinline__ uint64_t exp2_mufu2(uint32_t a, uint32_t b) {
+    return ptx::pack2(ptx::ex2_mufu(__uint_as_float(a)), ptx::ex2_mufu(__uint_as_float(b)));
+}
+
+// FMA pipe: 2^x = 2^j 2^f, j = round(x) by the 1.5*2^23 shift, f = x - j in
+// [-1/2, 1/2], 2^f by a degree-4 polynomial (relative error 3.6e-6; fitted by
+// flashdiffusion_b200/csrc/exp2_poly_fit.py), 2^j added into the exponent
+// field with one integer multiply-add.  x is clamped at -125 first so the
+// exponent field cannot underflow.
+__device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {
+    const float x0 = fmaxf(__uint_as_float(a), -125.0f);
+    const float x1 = fmaxf(__uint_as_float(b), -125.0f);
+    const uint64_t X = ptx::pack2(x0, x1);
+    const uint64_t SH = ptx::pack2(12582912.0f, 12582912.0f);
+    const uint64_t T = ptx::add2(X, SH);
+    const uint64_t F = ptx::sub2(X, ptx::sub2(T, SH));
+    uint64_t P = ptx::fma2(ptx::pack2(0.009782912f, 0.009782912f), F, ptx::pack2(0.055976883f, 0.055976883f));
+    P = ptx::fma2(P, F, ptx::pack2(0.2402071f, 0.2402071f));
+    P = ptx::fma2(P, F, ptx::pack2(0.6931136f, 0.6931136f));
+    P = ptx::fma2(P, F, ptx::pack2(1.0f, 1.0f));
+    uint32_t p0, p1, t0, t1;
+    ptx::unpack2(P, p0, p1);
+    ptx::unpack2(T, t0, t1);
+    // the low 9 bits of the shifted value hold j mod 512, so t << 23 == j << 23 (mod 2^32)
+    return ptx::pack2(__uint_as_float(p0 + (t0 << 23)), __uint_as_float(p1 + (t1 << 23)));
+}
+
+}  // namespace tc
+
+// Host helpers defined in fd_tc.cu.
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16);
+int num_sms();
+
+}  // namespace fd

@@ -240,3 +240,34 @@ def test_backend_contract():
     out = mv(st, v)
     assert out.dtype == np.float64
     assert rel_l2(out, M @ v) <= 2e-3
+
+
+@pytest.mark.parametrize("prec", ["f16", "bf16"])
+@pytest.mark.parametrize("nq,nk,d,r", [(3000, 20000, 64, 16), (2000, 9000, 128, 32), (700, 3000, 66, 40),
+                                       (257, 1100, 128, 64), (300, 2000, 3, 100)])
+def test_block_rhs_tensor_core_vs_oracle(prec, nq, nk, d, r):
+    """r > 1 on the tcgen05 path: O += P U as a second tensor-core GEMM (P fp16 in TMEM)."""
+    from flashdiffusion_b200 import FlashDiffusion
+    rng = np.random.default_rng(nq + nk + d + r)
+    K = rng.standard_normal((nk, d)).astype(np.float32)
+    Q = K[rng.integers(0, nk, nq)] + 0.2 * rng.standard_normal((nq, d)).astype(np.float32)
+    V = rng.standard_normal((nk, r)) * rng.uniform(1e-3, 1e3, r)[None, :]   # columns of very different scale
+    rq, rk = rng.uniform(0.5, 2, nq), rng.uniform(0.5, 2, nk)
+    beta = 1.0 / (2.0 * d)
+    ref = O.flash_diffusion(Q, K, V, beta, rq, rk)
+    out = FlashDiffusion(Q, K, V, beta, rq, rk, precision=prec)
+    assert out.shape == (nq, r)
+    for c in range(r):   # every column to the tolerance, whatever its scale
+        assert rel_l2(out[:, c], ref[:, c]) <= TOL[prec], c
+
+
+def test_block_rhs_smooth_eigvec_like_block():
+    """Configuration-5 shape class (d=128, r=32) on a smooth block (Ritz-vector-like)."""
+    from flashdiffusion_b200 import synthetic, GaussianOperator
+    X, beta = synthetic.tanh_manifold(n=40_000, d=128, seed=3)
+    op = GaussianOperator(X, None, beta, "f16")
+    V = np.cos(np.outer(X[:, 0].astype(np.float64), np.arange(32)) * 0.3)
+    out = op.apply(torch.from_numpy(V).cuda(), out_dtype=torch.float64).cpu().numpy()
+    rows = np.random.default_rng(0).choice(X.shape[0], 300, replace=False)
+    ref = O.flash_diffusion(X[rows], X, V, beta)
+    assert rel_l2(out[rows], ref) <= TOL["f16"]
