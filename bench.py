@@ -32,8 +32,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIGS = {
-    "c2": dict(workload="c2: DMAP matvec, Gaussian mixture N=200000 d=64, r=1, alpha=0.5", n=200_000, d=64),
-    "c5": dict(workload="c5: DMAP matvec, tanh manifold N=1000000 d=128, r=1, alpha=0.5", n=1_000_000, d=128),
+    "c2": dict(workload="c2: DMAP matvec, Gaussian mixture N=200000 d=64, r=1, alpha=0.5",
+               n=200_000, d=64, r=1, mode="dmap"),
+    "c3": dict(workload="c3: AMAP matvec (Q != K), 6-D manifold N_q=N_k=500000 d=64, r=1, alpha=0.5",
+               n=500_000, d=64, r=1, mode="amap"),
+    "c4": dict(workload="c4: Doob matvec, Langevin double well 500000 frames d=66, r=1, alpha=0.5",
+               n=500_000, d=66, r=1, mode="doob"),
+    "c5": dict(workload="c5: DMAP block matvec, tanh manifold N=1000000 d=128, r=32, alpha=0.5",
+               n=1_000_000, d=128, r=32, mode="dmap"),
 }
 
 
@@ -50,27 +56,36 @@ def parse():
 
 
 def make_data(cfg, seed=0):
+    """(Q, K or None, beta, h or None) for a configuration (seeded synthetic)."""
     from flashdiffusion_b200 import synthetic
+    c = CONFIGS[cfg]
     if cfg == "c2":
-        X, beta = synthetic.gaussian_mixture(n=CONFIGS[cfg]["n"], d=CONFIGS[cfg]["d"], seed=seed)
-    else:
-        X, beta = synthetic.tanh_manifold(n=CONFIGS[cfg]["n"], d=CONFIGS[cfg]["d"], seed=seed)
-    return X, beta
+        X, beta = synthetic.gaussian_mixture(n=c["n"], d=c["d"], seed=seed)
+        return X, None, beta, None
+    if cfg == "c3":
+        Q, K, beta = synthetic.amap_manifold(n=c["n"], d=c["d"], seed=seed)
+        return Q, K, beta, None
+    if cfg == "c4":
+        X, beta, h, _ = synthetic.langevin_trajectory(n_frames=c["n"], d=c["d"], seed=seed)
+        return X, None, beta, h
+    X, beta = synthetic.tanh_manifold(n=c["n"], d=c["d"], seed=seed)
+    return X, None, beta, None
 
 
-def cpu_sample(X, beta, rows, seed=0):
-    """Time the reference algorithm (NumPy tile loop) on `rows` seeded rows x all keys.
+def cpu_sample(Q, K, beta, rows, r=1, seed=0):
+    """Time the reference algorithm (NumPy tile loop) on `rows` seeded query rows x all keys.
 
-    Returns (evals/s, seconds, rows).  The DMAP scales are set to ones for the
-    sample: they cost O(N) and do not change the tile loop being timed."""
+    Returns (evals/s, seconds, rows).  The row/column scales are set to ones
+    for the sample: they cost O(N) and do not change the tile loop timed."""
     from oracle import fd_oracle as O
-    idx = np.sort(np.random.default_rng(seed).choice(X.shape[0], rows, replace=False))
-    v = np.random.default_rng(seed + 1).standard_normal((X.shape[0], 1))
-    O.flash_diffusion(X[idx[:64]], X[:4096], v[:4096], beta)          # warm BLAS threads
+    K = Q if K is None else K
+    idx = np.sort(np.random.default_rng(seed).choice(Q.shape[0], rows, replace=False))
+    v = np.random.default_rng(seed + 1).standard_normal((K.shape[0], r))
+    O.flash_diffusion(Q[idx[:64]], K[:4096], v[:4096], beta)          # warm BLAS threads
     t0 = time.perf_counter()
-    O.flash_diffusion(X[idx], X, v, beta)
+    O.flash_diffusion(Q[idx], K, v, beta)
     dt = time.perf_counter() - t0
-    return rows * X.shape[0] / dt, dt, rows
+    return rows * K.shape[0] / dt, dt, rows
 
 
 class ClockSampler:
@@ -136,22 +151,19 @@ def run_reference(args):
     if rank != 0:
         return
     cfg = CONFIGS[args.config]
-    X, beta = make_data(args.config)
+    Q, K, beta, _ = make_data(args.config)
     rows = args.cpu_rows or (256 if args.config == "c2" else 64)
     cores = os.cpu_count()
     for _ in range(args.warmup):
-        cpu_sample(X, beta, min(rows, 64))
-    vals = []
-    for s in range(args.steps):
-        ev, dt, _ = cpu_sample(X, beta, rows, seed=s)
-        vals.append(ev)
+        cpu_sample(Q, K, beta, min(rows, 64), cfg["r"])
+    vals = [cpu_sample(Q, K, beta, rows, cfg["r"], seed=s_)[0] for s_ in range(args.steps)]
     v = float(np.mean(vals))
     n = cfg["n"]
     line = {"impl": "reference", "metric": "kernel evals/sec per matvec (N^2/t)", "value": v, "unit": "evals/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * n * n / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 GEMM + f64 exp/accumulate", "data": "synthetic (seeded generator)",
-            "config": {"workload": cfg["workload"], "n": n, "d": cfg["d"], "sample_rows": rows,
+            "config": {"workload": cfg["workload"], "n": n, "d": cfg["d"], "r": cfg["r"], "sample_rows": rows,
                        "parallelism": "host BLAS threads"},
             "cpu_baseline": {"value": v, "unit": "evals/s", "cores": cores, "kind": "port",
                              "sample": f"{rows} seeded rows x all {n} keys per step, extrapolated to N^2"},
@@ -170,20 +182,25 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     from flashdiffusion_b200 import native
-    from flashdiffusion_b200.distributed import ShardedDMAP
+    from flashdiffusion_b200.distributed import ShardedOperator
     native.require_device(local)
     cfg = CONFIGS[args.config]
-    X, beta = make_data(args.config)
-    n, d = X.shape
+    Q, K, beta, h = make_data(args.config)
+    nq, d = Q.shape
+    nk = nq if K is None else K.shape[0]
+    r = cfg["r"]
     dev = torch.device("cuda", local)
-    Xd = torch.from_numpy(X).to(dev)
+    Qd = torch.from_numpy(Q).to(dev)
+    Kd = None if K is None else torch.from_numpy(K).to(dev)
+    hd = None if h is None else torch.from_numpy(h).to(dev)
 
-    # prepass (two Coifman-Lafon passes), timed once on the device
+    # operator set-up (packing) and the Coifman-Lafon prepass, timed on the device
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    op = ShardedDMAP(Xd, beta, 0.5, "f16")
+    op = ShardedOperator(Qd, Kd, beta, 0.5, "f16", mode=cfg["mode"], h=hd)
+    torch.cuda.synchronize()
     setup_s = time.perf_counter() - t0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -192,14 +209,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     prepass_s = e0.elapsed_time(e1) / 1e3
 
-    v = torch.from_numpy(np.random.default_rng(1).standard_normal(n)).to(dev)
+    shape = (nk,) if r == 1 else (nk, r)
+    v = torch.from_numpy(np.random.default_rng(1).standard_normal(shape)).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)     # 256 MB > 126 MB L2
 
-    def step():
-        return op.matvec_device(v)
-
     for _ in range(args.warmup):
-        step()
+        op.matvec_device(v)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -208,7 +223,6 @@ def run_ours(args):
     time.sleep(0.25)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kst = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ken = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     torch.cuda.synchronize()
     if world > 1:
@@ -220,22 +234,20 @@ def run_ours(args):
         ken[i].record()
         op.gather(vl)
         ends[i].record()
-        kst[i] = starts[i]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    step_ms = float(np.sum([s.elapsed_time(e) for s, e in zip(starts, ends)])) / args.steps
-    kern_ms = float(np.sum([s.elapsed_time(e) for s, e in zip(kst, ken)])) / args.steps
+    step_ms = float(np.sum([a.elapsed_time(b) for a, b in zip(starts, ends)])) / args.steps
+    kern_ms = float(np.sum([a.elapsed_time(b) for a, b in zip(starts, ken)])) / args.steps
     t = torch.tensor([step_ms, kern_ms, prepass_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms, kern_ms, prepass_s = [float(x) for x in t.cpu()]
 
-    # end to end through the public API with host buffers (N=1: DiffusionMap-style
-    # host matvec; N>1: each rank copies v in, runs its shard, gathers, copies out)
-    pinned_v = torch.from_numpy(np.random.default_rng(2).standard_normal(n)).pin_memory()
-    pinned_out = torch.empty(n, dtype=torch.float64).pin_memory()
+    # end to end with host buffers: pinned host V -> device, product (+ gather), result -> pinned host
+    pinned_v = torch.from_numpy(np.random.default_rng(2).standard_normal(shape)).pin_memory()
+    pinned_out = torch.empty((nq,) if r == 1 else (nq, r), dtype=torch.float64).pin_memory()
     for _ in range(2):
         pinned_out.copy_(op.matvec_device(pinned_v.to(dev, non_blocking=True)))
     torch.cuda.synchronize()
@@ -252,52 +264,59 @@ def run_ours(args):
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_s = float(e2e_s.item())
 
-    # Lanczos time to k=16 eigenpairs (bf16 tiles, device fp64 basis), outside the timed region
+    # Lanczos time to k eigenpairs (16-bit tiles, device fp64 basis), outside the timed region
     lanczos = None
-    if not args.no_lanczos:
+    if not args.no_lanczos and cfg["mode"] == "dmap" and r == 1:
         from flashdiffusion_b200.eigensolver import SolveInfo, trlan
         info = SolveInfo()
+        kk = 16
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        theta, _, res = trlan(op.matvec_device, n, 16, 1e-3, 200, 33, None, dev, info, stall_restarts=2)
+        theta, _, res = trlan(op.matvec_device, nq, kk, 1e-3, 200, 2 * kk + 1, None, dev, info, stall_restarts=2)
         torch.cuda.synchronize()
         lt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(lt, op=dist.ReduceOp.MAX)
-        lanczos = {"k": 16, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tiles": "f16",
-                   "max_rel_residual": float(np.max(res / np.abs(theta))), "top_eigenvalues": [float(x) for x in np.sort(theta)[::-1][:4]]}
+        lanczos = {"k": kk, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tiles": "f16",
+                   "tol": 1e-3, "max_rel_residual": float(np.max(res / np.abs(theta))),
+                   "top_eigenvalues": [float(x) for x in np.sort(theta)[::-1][:4]]}
 
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return
     hbm, bf16_tf, sm_max, peak_src = load_peaks()
-    evals = float(n) * float(n)
+    evals = float(nq) * float(nk)
     value = evals / (step_ms / 1e3)
     rows_local = op.rows[1] - op.rows[0]
-    kern_evals = float(rows_local) * n / (kern_ms / 1e3)
+    kern_evals = float(rows_local) * nk / (kern_ms / 1e3)
     sm_clock = (clk or {}).get("sm_mhz") or sm_max
-    mufu_peak = 16 * 148 * sm_max * 1e6              # ex2 per s at max SM clock (nominal rate)
-    tensor_peak_evals = bf16_tf * 1e12 / (2 * d)
+    flops_per_eval = 2 * d + (2 * r if r > 1 else 0)
+    mufu_peak = 16 * 148 * sm_max * 1e6          # ex2 per s at max SM clock (measured 15.9/clk/SM)
+    tensor_peak_evals = bf16_tf * 1e12 / flops_per_eval
     peak_evals = min(mufu_peak, tensor_peak_evals)
-    cpu_rows = args.cpu_rows or 256
-    cpu_ev, cpu_dt, _ = cpu_sample(X, beta, cpu_rows)
+    cpu_rows = args.cpu_rows or (256 if nk <= 200_000 else 64)
+    cpu_ev, cpu_dt, _ = cpu_sample(Q, K, beta, cpu_rows, r)
     line = {
         "metric": "kernel evals/sec per matvec (N^2/t)", "value": value, "unit": "evals/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 tiles, f32 accumulate", "data": "synthetic (seeded generator)",
-        "config": {"workload": cfg["workload"], "n": n, "d": d, "beta": beta, "tiles": "f16 tcgen05",
-                   "parallelism": f"row-shard x{world}, NCCL all-gather", "l2": "flushed between steps (256 MB write)"},
-        "roofline": {"bound": "mufu", "achieved": kern_evals, "peak": peak_evals, "unit": "evals/s",
-                     "frac": kern_evals / peak_evals, "traffic": None,
-                     "mufu_peak": "16 ex2/clk/SM x 148 SMs x %.0f MHz (nominal rate, max clock)" % sm_max,
-                     "tensor": {"achieved": kern_evals * 2 * d / 1e12, "peak": bf16_tf, "unit": "TFLOP/s",
-                                "frac": kern_evals * 2 * d / 1e12 / bf16_tf, "peak_source": peak_src},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 tiles, f32 accumulate",
+        "data": "synthetic (seeded generator)",
+        "config": {"workload": cfg["workload"], "n_q": nq, "n_k": nk, "d": d, "r": r, "beta": beta,
+                   "mode": cfg["mode"], "tiles": "f16 tcgen05", "parallelism": f"row-shard x{world}, NCCL all-gather",
+                   "l2": "flushed between steps (256 MB write)"},
+        "roofline": {"bound": "mufu" if mufu_peak <= tensor_peak_evals else "tensor", "achieved": kern_evals,
+                     "peak": peak_evals, "unit": "evals/s", "frac": kern_evals / peak_evals, "traffic": None,
+                     "peak_basis": "min(MUFU ex2 16/clk/SM x 148 SMs x %.0f MHz, measured bf16 %.0f TFLOP/s / %d flop per eval)"
+                                   % (sm_max, bf16_tf, flops_per_eval),
+                     "tensor": {"achieved": kern_evals * flops_per_eval / 1e12, "peak": bf16_tf, "unit": "TFLOP/s",
+                                "frac": kern_evals * flops_per_eval / 1e12 / bf16_tf, "peak_source": peak_src},
                      "frac_at_sampled_clock": kern_evals / min(16 * 148 * sm_clock * 1e6, tensor_peak_evals)},
         "cpu_baseline": {"value": cpu_ev, "unit": "evals/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{cpu_rows} seeded rows x all {n} keys (NumPy tile loop of the reference algorithm), {cpu_dt:.1f}s"},
-        "e2e": {"value": evals / e2e_s, "unit": "evals/s", "h2d_bytes_per_step": 8 * n, "d2h_bytes_per_step": 8 * n},
-        "gpu_launches": 3 * args.steps,
+                         "sample": f"{cpu_rows} seeded rows x all {nk} keys, r={r} (NumPy tile loop of the reference algorithm), {cpu_dt:.1f}s"},
+        "e2e": {"value": evals / e2e_s, "unit": "evals/s", "h2d_bytes_per_step": 8 * nk * r,
+                "d2h_bytes_per_step": 8 * nq * r},
+        "gpu_launches": (3 if r == 1 else 4) * args.steps,
         "prepass_s": prepass_s, "setup_s": setup_s, "kernel_ms": kern_ms,
         "lanczos": lanczos, "clocks": clk,
     }

@@ -113,3 +113,77 @@ class ShardedDMAP:
     def matvec_device(self, v: torch.Tensor) -> torch.Tensor:
         """Full M v on every rank: local rows + one all-gather."""
         return self.gather(self.matvec_local(v))
+
+
+class ShardedOperator:
+    """Row-sharded operator for the three reference modes, with one all-gather per product.
+
+    mode "dmap": Q = K = X, M = diag(rscale) K diag(rscale) (``FD/dmap.py:78-136``);
+    mode "amap": Q != K, rscale_k from the DMAP normalisation of K and the
+                 query scale of the reference's only Q != K normaliser
+                 (``FD/utils.py:92-102``);
+    mode "doob": DMAP with h: M_h v = M (h v) / (M h) (``FD/dmap.py:221-261``).
+    Every rank holds all of K and owns a contiguous block of 256-row tiles of Q.
+    """
+
+    def __init__(self, Q: torch.Tensor, K: Optional[torch.Tensor], beta: float, alpha: float,
+                 precision: str = "f16", mode: str = "dmap", h: Optional[torch.Tensor] = None, group=None):
+        from . import native
+        from .kernel import GaussianOperator
+        if mode not in ("dmap", "amap", "doob"):
+            raise ValueError(f"mode must be dmap, amap or doob (got {mode!r})")
+        if mode == "doob" and h is None:
+            raise ValueError("mode 'doob' needs h")
+        self.mode = mode
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.group = group
+        self.alpha = alpha
+        Kx = Q if K is None else K
+        self.nq, self.nk = Q.shape[0], Kx.shape[0]
+        self.rows = shard_rows(self.nq, self.world, self.rank)
+        self.gather = RowGather(self.nq, self.world, group)
+        shift = native.mean_rows(Kx)
+        a, b = self.rows
+        self.op = GaussianOperator(Q[a:b], Kx, beta, precision, shift=shift)
+        if mode == "amap":
+            self.krows = shard_rows(self.nk, self.world, self.rank)
+            self.kgather = RowGather(self.nk, self.world, group)
+            ka, kb = self.krows
+            self.kop = GaussianOperator(Kx[ka:kb], Kx, beta, precision, shift=shift)
+        self.h = None if h is None else h.to(torch.float32).contiguous()
+        self.rscale_q = self.rscale_k = self.ph = None
+
+    def fit(self):
+        """Coifman-Lafon prepasses (two all-gathers each for the key side)."""
+        from . import native
+        if self.mode == "amap":
+            Dk = self.kgather(self.kop.apply(out_dtype=torch.float32)[:, 0].contiguous()).contiguous()
+            wk = native.dmap_weights(Dk, self.alpha)
+            Kw = self.kgather(self.kop.apply(wk, out_dtype=torch.float32)[:, 0].contiguous()).contiguous()
+            _, self.rscale_k = native.dmap_rscale(Kw, wk)
+            Dq = self.op.apply(wk, out_dtype=torch.float32)[:, 0].contiguous()      # D_q = K(Q,K) w_k
+            wq = native.dmap_weights(Dq, self.alpha)
+            _, self.rscale_q = native.dmap_rscale(Dq, wq)                          # this rank's rows
+        else:
+            D = self.gather(self.op.apply(out_dtype=torch.float32)[:, 0].contiguous()).contiguous()
+            w = native.dmap_weights(D, self.alpha)
+            Kw = self.gather(self.op.apply(w, out_dtype=torch.float32)[:, 0].contiguous()).contiguous()
+            _, rs = native.dmap_rscale(Kw, w)
+            a, b = self.rows
+            self.rscale_k, self.rscale_q = rs, rs[a:b].contiguous()
+            if self.mode == "doob":
+                self.ph = self.op.apply(self.h, col_scale=rs, row_scale=self.rscale_q,
+                                        out_dtype=torch.float32)[:, 0].contiguous()
+        return self
+
+    def matvec_local(self, v: torch.Tensor, out_dtype=torch.float64) -> torch.Tensor:
+        squeeze = v.dim() == 1
+        out = self.op.apply(v[:, None] if squeeze else v, col_scale=self.rscale_k, col_h=self.h,
+                            row_scale=self.rscale_q, row_div=self.ph, out_dtype=out_dtype)
+        return out[:, 0] if squeeze else out
+
+    def matvec_device(self, v: torch.Tensor) -> torch.Tensor:
+        """Full product on every rank: this rank's rows + one all-gather."""
+        return self.gather(self.matvec_local(v))
+
