@@ -52,7 +52,12 @@ def parse():
     p.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     p.add_argument("--no-lanczos", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU sample (0 = auto)")
-    return p.parse_args()
+    p.add_argument("--n", type=int, default=0, help="override the number of points (small profiling cases)")
+    a = p.parse_args()
+    if a.n:
+        for c in CONFIGS.values():
+            c["n"] = a.n
+    return a
 
 
 def make_data(cfg, seed=0):

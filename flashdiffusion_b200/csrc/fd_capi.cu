@@ -137,7 +137,8 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
                  "workspace must be non-null and 256-byte aligned");
     if (nq == 0) return FD_OK;
 
-    const int cpl = cols_per_launch(tile, r);
+    // (the workspace query is sized for 64 block columns, an upper bound for any d)
+    const int cpl = (is_tc_tile(tile) && r > 1) ? block_max_cols(d) : cols_per_launch(tile, r);
     const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
     uint8_t* ws = (uint8_t*)workspace;
     float* u = (float*)ws;

@@ -53,6 +53,7 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
 
 // 16-bit tcgen05 tiles with a block right-hand side (up to 64 columns per launch).
 int block_rp(int rc);
+int block_max_cols(int d);
 size_t tc_block_workspace_bytes(int rp);
 int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile, const void* ut,
                     int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes,

@@ -6,8 +6,10 @@
 //                           fp16 parts written back to TMEM over S columns each
 //                           warpgroup has already read)
 //   O += P_hi U_hi + P_hi U_lo + P_lo U_hi
-//                          (three tcgen05.mma per 16 keys, A from TMEM, B = U^T
-//                           tiles in shared memory): fp32-class products from
+//                          (two tcgen05.mma per 16 keys, A from TMEM: P_hi times
+//                           the stacked [U_hi; U_lo] tile (N = 2r) into two
+//                           accumulator halves, then P_lo U_hi; the halves are
+//                           summed when O is read): fp32-class products from
 //                           fp16 operands, so the block path keeps the accuracy
 //                           of the r = 1 path (which multiplies in fp32)
 //
@@ -16,14 +18,17 @@
 // scale is undone in the output epilogue).  There is no online softmax: the row scale is a
 // known vector, applied once per output row.
 //
-// CTA = 128 query rows x stream of 128-key tiles.  Warp roles (18 warps):
-//   warps 0-15  four epilogue warpgroups WG(p, h): parity p of the key tile
-//               (TMEM S/P buffer p) and column half h of it
+// CTA = 128 query rows x stream of 96-key tiles.  Warp roles (18 warps):
+//   warps 0-15  four epilogue warpgroups; warpgroup w exponentiates the key
+//               tiles m = w (mod 4) in its own TMEM S/P buffer (4 x 96 columns,
+//               plus up to 64 columns of O: 448 of the 512 TMEM columns)
 //   warp  16    TMA producer: query tile per row tile; per key tile the K
-//               box(es) and the 64-key boxes of U_hi^T and U_lo^T (no multicast)
-//   warp  17    MMA issuer: Q.K^T of tile m, then P.U of tile m-1 (so the
-//               tensor pipe never waits for one epilogue), all P.U products
-//               of a row tile accumulating into ONE TMEM accumulator O
+//               box(es) into the K ring and the 64-key boxes of U_hi^T and
+//               U_lo^T into the U ring (no multicast)
+//   warp  17    Q.K^T issuer (up to four S tiles ahead of the epilogue)
+//   warps 18-19 P.U issuers, one per accumulator chain: each tcgen05.mma
+//               costs its issuing thread about 100 cycles whatever its size,
+//               so the three independent chains get three issuing warps
 // The persistent work split and the deterministic cross-CTA fix-up are the
 // ones of the r = 1 kernel (fd_tc.cu).
 #include "fd_tc_common.cuh"
@@ -31,32 +36,60 @@
 namespace fd {
 namespace tcb {
 
+// Optional wait-time accounting (build with -DFD_PROFILE_WAITS): cycles that
+// lane 0 of each warp of CTA 0 spends in each pipeline wait, by wait site.
+#ifdef FD_PROFILE_WAITS
+__device__ unsigned long long g_wait_cycles[16];
+__device__ __forceinline__ bool timed_wait(int slot, uint64_t* b, uint32_t ph, volatile int* a, int* st,
+                                           uint64_t lim) {
+    const long long t0 = clock64();
+    const bool ok = ptx::wait_bounded(b, ph, a, st, lim);
+    if (blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+        atomicAdd(&g_wait_cycles[slot], (unsigned long long)(clock64() - t0));
+    return ok;
+}
+#define FD_WAIT(slot, ...) timed_wait(slot, __VA_ARGS__)
+#else
+#define FD_WAIT(slot, ...) ptx::wait_bounded(__VA_ARGS__)
+#endif
+
 using tc::Sched;
 
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = 96;                     // keys per tile (N of Q.K^T, K of P.U)
 constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;
-constexpr int NTHREADS = 18 * 32;
-constexpr uint32_t BOX_BYTES = 128 * 128;  // 128 rows x 64 16-bit columns
+constexpr int MMA_WARP = 17;               // Q.K^T issuer (and TMEM owner)
+constexpr int PV_WARP0 = 18;               // P_hi . [U_hi; U_lo] issuer
+constexpr int PV_WARP1 = 19;               // P_lo . U_hi issuer
+constexpr int NTHREADS = 20 * 32;
+constexpr uint32_t BOX_BYTES = 128 * 128;  // query box: 128 rows x 64 16-bit columns
+constexpr uint32_t KBOX_BYTES = BN * 128;  // key box: BN rows x 64 16-bit columns
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t O_COL = 256;            // O accumulator columns [256, 256 + RP)
+constexpr int NSB = 4;                     // TMEM S/P buffers of BN columns, one per epilogue warpgroup
+constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 3 RP)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 template <int KB, int RP>
 struct Cfg {
     static constexpr uint32_t Q_BYTES = KB * BOX_BYTES;
     static constexpr uint32_t UT_BOX = RP * 128;                 // RP rows x 64 keys
-    static constexpr uint32_t STAGE_BYTES = KB * BOX_BYTES + 4 * UT_BOX;   // K, U_hi^T (2 boxes), U_lo^T (2)
-    static constexpr int STAGES_RAW = (int)((222u * 1024u - Q_BYTES) / STAGE_BYTES);
-    static constexpr int STAGES = STAGES_RAW > 6 ? 6 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
-    static constexpr uint32_t BAR_OFF = Q_BYTES + STAGES * STAGE_BYTES;
-    // kfull[S], kempty[S], qfull, qempty, sfull[2], sempty[2], pfull[2], ofull, oempty, done
-    static constexpr int NBARS = 2 * STAGES + 2 + 6 + 3;
+    // two rings: K tiles (released as soon as Q.K^T is done) and U^T tiles
+    // (U_hi^T and U_lo^T, 2 boxes each; released after P.U, i.e. after the epilogue)
+    static constexpr uint32_t STAGE_BYTES = KB * KBOX_BYTES;
+    static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX;
+    static constexpr uint32_t BUDGET = 222u * 1024u - Q_BYTES;
+    static constexpr int USTAGES = 4;              // U^T tiles live from their load to their P.U
+    static constexpr int K_RAW = (int)((BUDGET - USTAGES * USTAGE_BYTES) / STAGE_BYTES);
+    static constexpr int STAGES = K_RAW > 6 ? 6 : (K_RAW < 2 ? 2 : K_RAW);
+    static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
+    static constexpr uint32_t BAR_OFF = U_OFF + USTAGES * USTAGE_BYTES;
+    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4], pfull[4], ofull, oempty, done[3]
+    static constexpr int NBARS = 2 * STAGES + 2 * USTAGES + 2 + 3 * NSB + 5;
     static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t SMEM_BYTES = MISC_OFF + 16;
     static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
     static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
+    static_assert(O_COL + 3 * RP <= TMEM_COLS, "TMEM budget");
 };
 
 // Load `RP / 4` consecutive O columns of this thread's row.
@@ -119,7 +152,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                 const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
                 int64_t nq, int kd, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
-                double* __restrict__ part, int* __restrict__ status) {
+                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2) {
     using C = Cfg<KB, RP>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -128,12 +161,14 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     uint64_t* bars = (uint64_t*)(base + C::BAR_OFF);
     uint64_t* kfull = bars;
     uint64_t* kempty = kfull + C::STAGES;
-    uint64_t* qfull = kempty + C::STAGES;
+    uint64_t* ufull = kempty + C::STAGES;
+    uint64_t* uempty = ufull + C::USTAGES;
+    uint64_t* qfull = uempty + C::USTAGES;
     uint64_t* qempty = qfull + 1;
     uint64_t* sfull = qfull + 2;
-    uint64_t* sempty = sfull + 2;
-    uint64_t* pfull = sempty + 2;
-    uint64_t* ofull = pfull + 2;
+    uint64_t* sempty = sfull + NSB;
+    uint64_t* pfull = sempty + NSB;
+    uint64_t* ofull = pfull + NSB;
     uint64_t* oempty = ofull + 1;
     uint64_t* done = oempty + 1;
     uint32_t* tmem_slot = (uint32_t*)(base + C::MISC_OFF);
@@ -145,22 +180,29 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
     const int64_t n_jt = sc.n_jt;
     const int ksteps = kd / 16;
+#ifdef FD_PROFILE_WAITS
+    const long long t_start = clock64();
+#endif
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::STAGES; ++i) {
             ptx::mbar_init(&kfull[i], 1);
             ptx::mbar_init(&kempty[i], 1);
         }
+        for (int i = 0; i < C::USTAGES; ++i) {
+            ptx::mbar_init(&ufull[i], 1);
+            ptx::mbar_init(&uempty[i], 2);   // both P.U issuers
+        }
         ptx::mbar_init(qfull, 1);
         ptx::mbar_init(qempty, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < NSB; ++i) {
             ptx::mbar_init(&sfull[i], 1);
-            ptx::mbar_init(&sempty[i], 1);
-            ptx::mbar_init(&pfull[i], 8);   // the 8 epilogue warps of one parity
+            ptx::mbar_init(&sempty[i], 2);   // both P.U issuers
+            ptx::mbar_init(&pfull[i], 4);   // the 4 warps of the warpgroup owning buffer i
         }
-        ptx::mbar_init(ofull, 1);
+        ptx::mbar_init(ofull, 2);           // both P.U issuers
         ptx::mbar_init(oempty, 16);         // every epilogue warp reads its share of O
-        ptx::mbar_init(done, 1);
+        for (int i = 0; i < 3; ++i) ptx::mbar_init(&done[i], 1);   // one per MMA issuer
         *abort = 0;
         ptx::fence_mbar_init();
     }
@@ -180,106 +222,115 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
 
     if (warp == TMA_WARP) {
         if (lane == 0) {
-            int stage = 0;
-            uint32_t kph = 0, qcount = 0;
+            int stage = 0, ustage = 0;
+            uint32_t kph = 0, uph = 0, qcount = 0;
             int64_t cur_rt = -1;
             int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            uint8_t* sU = base + C::U_OFF;
             for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
                 if (rt != cur_rt) {
-                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    if (qcount > 0 && !FD_WAIT(0, qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
                     for (int kb = 0; kb < KB; ++kb)
                         ptx::tma_load_2d(sQ + kb * BOX_BYTES, &tmq, qfull, kb * 64, (int)(rt * BM));
                     cur_rt = rt;
                     ++qcount;
                 }
-                if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                if (!FD_WAIT(1, &kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 uint8_t* st = sK + stage * C::STAGE_BYTES;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
                 for (int kb = 0; kb < KB; ++kb)
-                    ptx::tma_load_2d(st + kb * BOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                    ptx::tma_load_2d(st + kb * KBOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
                 // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
+                if (!FD_WAIT(2, &uempty[ustage], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                uint8_t* su = sU + ustage * C::USTAGE_BYTES;
+                ptx::mbar_expect_tx(&ufull[ustage], C::USTAGE_BYTES);
                 for (int part2 = 0; part2 < 2; ++part2)
                     for (int h = 0; h < 2; ++h)
-                        ptx::tma_load_2d(st + KB * BOX_BYTES + (part2 * 2 + h) * C::UT_BOX, &tmu, &kfull[stage],
+                        ptx::tma_load_2d(su + (h * 2 + part2) * C::UT_BOX, &tmu, &ufull[ustage],
                                          (int)(jt * BN + h * 64), part2 * RP);
-                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
             }
         }
     } else if (warp == MMA_WARP) {
+        // ---- Q.K^T issuer ---------------------------------------------------
         if (lane == 0) {
             const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
             int stage = 0;
-            uint32_t kph = 0, qcount = 0, ocount = 0;
+            uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
             int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            // the P.U product of the previous tile, issued after the next Q.K^T
-            bool have_pend = false, pend_last = false, fresh = true;
-            int pend_stage = 0;
-            int64_t pend_m = 0;
-            auto issue_pv = [&]() -> bool {
-                const int pb = (int)(pend_m & 1);
-                if (!ptx::wait_bounded(&pfull[pb], (uint32_t)((pend_m >> 1) & 1), abort, status, WAIT_LIMIT_NS)) return false;
-                if (fresh && !ptx::wait_bounded(oempty, (ocount & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) return false;
+            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+                const int64_t m = n - n0;
+                const int b = (int)(m % NSB);
+                if (rt != cur_rt) {
+                    if (!FD_WAIT(6, qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    ++qcount;
+                    cur_rt = rt;
+                }
+                if (!FD_WAIT(7, &kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
+                if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
                 ptx::tc_fence_after();
-                const uint32_t ut = k_base + pend_stage * C::STAGE_BYTES + KB * BOX_BYTES;
-#pragma unroll 1
+                const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                for (int ks = 0; ks < ksteps; ++ks) {
+                    const uint32_t kc = (ks & 3) * 32;
+                    ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + (ks >> 2) * BOX_BYTES + kc),
+                                 ptx::sw128_kmajor_desc(ka + (ks >> 2) * KBOX_BYTES + kc), idesc_qk, ks > 0);
+                }
+                ptx::umma_commit(&sfull[b]);
+                ptx::umma_commit(&kempty[stage]);
+                if ((n + 1 == n1) || (jt + 1 == n_jt)) ptx::umma_commit(qempty);
+                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+            ptx::umma_commit(done);
+            FD_WAIT(11, done, 0, abort, status, WAIT_LIMIT_NS);
+        }
+    } else if (warp == PV_WARP0 || warp == PV_WARP1) {
+        // ---- P.U issuers: warp PV_WARP0 runs O1 += P_hi [U_hi; U_lo] (N = 2 RP),
+        //      warp PV_WARP1 runs O2 += P_lo U_hi (N = RP); each tcgen05.mma costs
+        //      its issuing thread ~100 cycles, so independent chains get their
+        //      own issuing warps
+        if (lane == 0) {
+            const int t = warp - PV_WARP0;
+            const uint32_t u_base = ptx::smem_u32(base + C::U_OFF);
+            const uint32_t idesc = t == 0 ? idesc_pv2 : idesc_pv;
+            const uint32_t dcol = tmem + O_COL + (t == 0 ? 0u : 2u * RP);
+            int ustage = 0;
+            uint32_t uph = 0, ocount = 0;
+            bool fresh = true;
+            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
+            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+                const int64_t m = n - n0;
+                const int pb = (int)(m % NSB);
+                if (!FD_WAIT(3, &ufull[ustage], uph, abort, status, WAIT_LIMIT_NS)) break;
+                if (!FD_WAIT(4, &pfull[pb], (uint32_t)((m / NSB) & 1), abort, status, WAIT_LIMIT_NS)) break;
+                if (fresh && !FD_WAIT(5, oempty, (ocount & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                ptx::tc_fence_after();
+                const uint32_t ut = u_base + ustage * C::USTAGE_BYTES;
                 for (int ks = 0; ks < BN / 16; ++ks) {
-                    const uint32_t off = (ks >> 2) * C::UT_BOX + (ks & 3) * 32;
-                    const uint64_t uhi = ptx::sw128_kmajor_desc(ut + off);
-                    const uint64_t ulo = ptx::sw128_kmajor_desc(ut + 2 * C::UT_BOX + off);
+                    // U_hi^T rows then U_lo^T rows of this 64-key box: one 2 RP-row operand
+                    const uint32_t off = (ks >> 2) * 2 * C::UT_BOX + (ks & 3) * 32;
                     // keys 16ks..16ks+15: P_hi in 8 columns, P_lo in the next 8
-                    const uint32_t ahi = tmem + pb * BN + ks * 16;
-                    ptx::umma_ts(tmem + O_COL, ahi, uhi, idesc_pv, (fresh && ks == 0) ? 0u : 1u);
-                    ptx::umma_ts(tmem + O_COL, ahi, ulo, idesc_pv, 1u);
-                    ptx::umma_ts(tmem + O_COL, ahi + 8, uhi, idesc_pv, 1u);
+                    const uint32_t a = tmem + pb * BN + ks * 16 + (t == 0 ? 0u : 8u);
+                    ptx::umma_ts(dcol, a, ptx::sw128_kmajor_desc(ut + off), idesc, (fresh && ks == 0) ? 0u : 1u);
                 }
                 fresh = false;
                 ptx::umma_commit(&sempty[pb]);
-                ptx::umma_commit(&kempty[pend_stage]);
-                if (pend_last) {
+                ptx::umma_commit(&uempty[ustage]);
+                if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
+                if ((n + 1 == n1) || (jt + 1 == n_jt)) {
                     ptx::umma_commit(ofull);
                     fresh = true;
                     ++ocount;
                 }
-                return true;
-            };
-            bool ok = true;
-            for (int64_t n = n0; n < n1 && ok; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-                const int64_t m = n - n0;
-                const int b = (int)(m & 1);
-                if (rt != cur_rt) {
-                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
-                    ++qcount;
-                    cur_rt = rt;
-                }
-                if (!ptx::wait_bounded(&kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
-                if (!ptx::wait_bounded(&sempty[b], (uint32_t)(((m >> 1) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
-                ptx::tc_fence_after();
-                const uint32_t ka = k_base + stage * C::STAGE_BYTES;
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
-                    ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + off),
-                                 ptx::sw128_kmajor_desc(ka + off), idesc_qk, ks > 0);
-                }
-                ptx::umma_commit(&sfull[b]);
-                const bool last = (n + 1 == n1) || (jt + 1 == n_jt);
-                if (last) ptx::umma_commit(qempty);
-                if (have_pend) ok = issue_pv();
-                have_pend = true;
-                pend_m = m;
-                pend_stage = stage;
-                pend_last = last;
-                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
-            if (ok && have_pend) issue_pv();
-            ptx::umma_commit(done);
-            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
+            ptx::umma_commit(&done[1 + t]);
+            FD_WAIT(11, &done[1 + t], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else {
         // ---- epilogue warpgroups ------------------------------------------
-        const int wg = warp >> 2;
-        const int p = wg & 1, h = wg >> 1;
+        const int wg = warp >> 2;             // key quarter of every tile, and O column quarter
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -289,42 +340,47 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
         for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
             const int64_t m = n - n0;
-            if ((int)(m & 1) == p) {
-                if (!ptx::wait_bounded(&sfull[p], (uint32_t)((m >> 1) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+            if ((int)(m % NSB) == wg) {
+                const int b = wg;
+                if (!FD_WAIT(9, &sfull[b], (uint32_t)((m / NSB) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
-                // S columns of this half; the 16 keys of chunk c come back as
-                // P_hi (8 columns) and P_lo (8 columns) over the same 16 S
-                // columns, which this thread has read before it writes them
-                const uint32_t tb = t_lane + p * BN + h * 64;
+                // the whole tile: the 16 keys of chunk c come back as P_hi (8
+                // columns) and P_lo (8 columns) over the same 16 S columns,
+                // which this thread has read before it writes them
+                const uint32_t tb = t_lane + b * BN;
                 uint32_t va[16], vb[16], ph[8], pl[8];
                 ptx::tmem_ld16(tb, va);
                 ptx::tmem_wait_ld16(va);
 #pragma unroll 1
-                for (int c = 0; c < 4; c += 2) {
+                for (int c = 0; c < BN / 16; c += 2) {
                     ptx::tmem_ld16(tb + (c + 1) * 16, vb);
                     exp2_to_f16x2(va, ph, pl);
                     tmem_st8(tb + c * 16, ph);
                     tmem_st8(tb + c * 16 + 8, pl);
                     ptx::tmem_wait_ld16(vb);
-                    if (c + 2 < 4) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                    if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
                     exp2_to_f16x2(vb, ph, pl);
                     tmem_st8(tb + (c + 1) * 16, ph);
                     tmem_st8(tb + (c + 1) * 16 + 8, pl);
-                    if (c + 2 < 4) ptx::tmem_wait_ld16(va);
+                    if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
                 }
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(&pfull[p]);
+                if (lane == 0) ptx::mbar_arrive(&pfull[b]);
             }
             if (n + 1 == n1 || jt + 1 == n_jt) {
                 // read this warpgroup's quarter of the O columns, scale, store
-                if (!ptx::wait_bounded(ofull, segs & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                if (!FD_WAIT(10, ofull, segs & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
                 constexpr int NC = RP / 4;
                 const int c0 = wg * NC;
-                float o[NC];
-                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);
+                float o[NC], o2[NC], o3[NC];
+                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);             // P_hi U_hi
+                tmem_ld_cols<NC>(t_lane + O_COL + RP + c0, o2);       // P_hi U_lo
+                tmem_ld_cols<NC>(t_lane + O_COL + 2 * RP + c0, o3);   // P_lo U_hi
+#pragma unroll
+                for (int i = 0; i < NC; ++i) o[i] += o2[i] + o3[i];
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(oempty);
@@ -347,6 +403,9 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         ptx::tc_fence_before();
     }
     __syncthreads();
+#ifdef FD_PROFILE_WAITS
+    if (cta == 0 && threadIdx.x == 0) atomicAdd(&g_wait_cycles[15], (unsigned long long)(clock64() - t_start));
+#endif
     if (warp == MMA_WARP) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, TMEM_COLS);
@@ -400,10 +459,15 @@ static int launch_block_t(const CUtensorMap& mq, const CUtensorMap& mk, const CU
     FD_CUDA_TRY(cudaFuncSetAttribute(tcb::tc_block_kernel<KB, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
     tcb::tc_block_kernel<KB, RP><<<sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, mu, colscale, rc, nq, kd, iqk,
-                                                                               ipv, sc, ep, part, status);
+                                                                               ipv, sc, ep, part, status,
+                                                                               ptx::idesc_f32acc(tcb::BM, 2 * RP, true));
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
+
+// Columns of U per launch: the three accumulator blocks (3 x 32) fit next to
+// the four 96-column S buffers in the 512 TMEM columns.
+int block_max_cols(int d) { (void)d; return 32; }
 
 template <int KB>
 static int launch_block_kb(int rp, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mu,
@@ -412,7 +476,7 @@ static int launch_block_kb(int rp, const CUtensorMap& mq, const CUtensorMap& mk,
     switch (rp) {
         case 16: return launch_block_t<KB, 16>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
         case 32: return launch_block_t<KB, 32>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
-        default: return launch_block_t<KB, 64>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
+        default: return set_error(FD_ERR_UNSUPPORTED, "block tile path: at most 32 columns per launch");
     }
 }
 
@@ -423,7 +487,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
                     cudaStream_t s) {
     if (nq == 0) return FD_OK;
     if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
-    FD_CHECK_ARG(rc >= 1 && rc <= 64, "block tile path: %d columns per launch (max 64)", rc);
+    FD_CHECK_ARG(rc >= 1 && rc <= 32, "block tile path: %d columns per launch (max 32)", rc);
     const int rp = block_rp(rc);
     const int kd = kd_bf16(d);
     const int kb = (int)cdiv(kd, 64);
@@ -454,3 +518,13 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
 }
 
 }  // namespace fd
+
+#ifdef FD_PROFILE_WAITS
+// Read and clear the wait-time counters of the block kernel (profiling builds only).
+extern "C" int fd_debug_wait_cycles(unsigned long long* host16) {
+    FD_CUDA_TRY(cudaMemcpyFromSymbol(host16, fd::tcb::g_wait_cycles, 16 * sizeof(unsigned long long)));
+    unsigned long long z[16] = {0};
+    FD_CUDA_TRY(cudaMemcpyToSymbol(fd::tcb::g_wait_cycles, z, sizeof(z)));
+    return FD_OK;
+}
+#endif
