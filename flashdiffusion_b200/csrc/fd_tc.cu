@@ -16,7 +16,8 @@
 //   warp  16    TMA producer: query tile once per row tile, key tiles through
 //               a STAGES-deep shared-memory ring (no multicast), and the
 //               matching 128 values of u through a 4-deep ring (bulk copies)
-//   warp  17    MMA issuer: tcgen05.mma kind::f16, M=128 N=128 K=16 steps
+//   warps 17-18 MMA issuers, one per query subtile: tcgen05.mma kind::f16,
+//               M=128 N=128 K=16 steps
 // Work split: the (row tile, key tile) pairs are cut into gridDim.x contiguous
 // ranges (persistent CTAs, one per SM).  A row tile fully inside one range is
 // written directly; a row tile cut between ranges leaves fp64 partials in the
@@ -36,8 +37,8 @@ constexpr int NSUB = 2;     // subtiles per CTA
 constexpr int ROWS = BM * NSUB;
 constexpr int BN = 128;     // key rows per tile = S columns
 constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;
-constexpr int NTHREADS = 18 * 32;
+constexpr int MMA_WARP = 17;    // MMA issuer of query subtile 0 (and TMEM owner); warp 18 issues subtile 1
+constexpr int NTHREADS = 19 * 32;
 constexpr uint32_t BOX_BYTES = 128 * 128;  // one 128-row x 64-col 16-bit box (128-byte rows)
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int URING = 4;                    // depth of the right-hand-side ring
@@ -52,8 +53,8 @@ struct Cfg {
     static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
     static constexpr uint32_t BAR_OFF = U_OFF + URING * U_BYTES;
     // barriers: kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4],
-    //           rfull[2], rempty[2], done
-    static constexpr int NBARS = 2 * STAGES + 2 * URING + 2 + 8 + 4 + 1;
+    //           rfull[2], rempty[2], done[2]
+    static constexpr int NBARS = 2 * STAGES + 2 * URING + 2 + 8 + 4 + 2;
     static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t RED_OFF = (MISC_OFF + 16 + 15) & ~15u;
     static constexpr uint32_t SMEM_BYTES = RED_OFF + NSUB * BM * 8;
@@ -115,14 +116,14 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::STAGES; ++i) {
             ptx::mbar_init(&kfull[i], 1);
-            ptx::mbar_init(&kempty[i], 1);
+            ptx::mbar_init(&kempty[i], 2);  // both MMA issuers
         }
         for (int i = 0; i < URING; ++i) {
             ptx::mbar_init(&ufull[i], 1);
             ptx::mbar_init(&uempty[i], 8);  // the 8 epilogue warps of one parity
         }
         ptx::mbar_init(qfull, 1);
-        ptx::mbar_init(qempty, 1);
+        ptx::mbar_init(qempty, 2);          // both MMA issuers
         for (int i = 0; i < 4; ++i) {
             ptx::mbar_init(&sfull[i], 1);
             ptx::mbar_init(&sempty[i], 4);  // one arrive per epilogue warp
@@ -131,7 +132,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             ptx::mbar_init(&rfull[i], BM);
             ptx::mbar_init(&rempty[i], BM);
         }
-        ptx::mbar_init(done, 1);
+        ptx::mbar_init(&done[0], 1);
+        ptx::mbar_init(&done[1], 1);
         *abort = 0;
         ptx::fence_mbar_init();
     }
@@ -180,8 +182,12 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 ptx::bulk_load(sU + us * BN, u + jt * BN, U_BYTES, &ufull[us]);
             }
         }
-    } else if (warp == MMA_WARP) {
+    } else if (warp == MMA_WARP || warp == MMA_WARP + 1) {
+        // one issuing warp per query subtile: a tcgen05.mma costs its issuing
+        // thread about 100 cycles whatever its size, so the two independent
+        // Q.K^T chains of a key tile get two issuers
         if (lane == 0) {
+            const int s = warp - MMA_WARP;
             const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
@@ -197,10 +203,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     cur_rt = rt;
                 }
                 if (!ptx::wait_bounded(&kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
-                bool ok = true;
-                for (int s = 0; s < NSUB && ok; ++s) {
+                {
                     const int b = s * 2 + p;
-                    if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::tc_fence_after();
                     const uint32_t qa = q_base + s * KB * BOX_BYTES;
                     const uint32_t ka = k_base + stage * C::STAGE_BYTES;
@@ -211,14 +216,13 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     }
                     ptx::umma_commit(&sfull[b]);
                 }
-                if (!ok) break;
                 ptx::umma_commit(&kempty[stage]);
                 if (n + 1 == n1 || jt + 1 == n_jt) ptx::umma_commit(qempty);
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
             // every MMA issued above has completed once `done` flips
-            ptx::umma_commit(done);
-            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
+            ptx::umma_commit(&done[s]);
+            ptx::wait_bounded(&done[s], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else {
         // ---- epilogue warpgroups ------------------------------------------
