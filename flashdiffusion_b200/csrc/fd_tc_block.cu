@@ -18,17 +18,17 @@
 // scale is undone in the output epilogue).  There is no online softmax: the row scale is a
 // known vector, applied once per output row.
 //
-// CTA = 128 query rows x stream of 96-key tiles.  Warp roles (18 warps):
-//   warps 0-15  four epilogue warpgroups; warpgroup w exponentiates the key
-//               tiles m = w (mod 4) in its own TMEM S/P buffer (4 x 96 columns,
-//               plus up to 64 columns of O: 448 of the 512 TMEM columns)
-//   warp  16    TMA producer: query tile per row tile; per key tile the K
+// CTA = 128 query rows x stream of 128-key tiles.  Warp roles (18 warps):
+//   warps 0-11  three epilogue warpgroups; warpgroup w exponentiates the key
+//               tiles m = w (mod 3) in its own TMEM S/P buffer (3 x 128 columns,
+//               plus 3 x 32 accumulator columns: 480 of the 512 TMEM columns)
+//   warp  12    TMA producer: query tile per row tile; per key tile the K
 //               box(es) into the K ring and the 64-key boxes of U_hi^T and
 //               U_lo^T into the U ring (no multicast)
-//   warp  17    Q.K^T issuer (up to four S tiles ahead of the epilogue)
-//   warps 18-19 P.U issuers, one per accumulator chain: each tcgen05.mma
+//   warps 13-14 Q.K^T issuers (even / odd tiles)
+//   warps 15-16 P.U issuers, one per accumulator chain: each tcgen05.mma
 //               costs its issuing thread about 100 cycles whatever its size,
-//               so the three independent chains get three issuing warps
+//               so independent chains get their own issuing warps
 // The persistent work split and the deterministic cross-CTA fix-up are the
 // ones of the r = 1 kernel (fd_tc.cu).
 #include "fd_tc_common.cuh"
@@ -56,17 +56,19 @@ __device__ __forceinline__ bool timed_wait(int slot, uint64_t* b, uint32_t ph, v
 using tc::Sched;
 
 constexpr int BM = 128;
-constexpr int BN = 96;                     // keys per tile (N of Q.K^T, K of P.U)
-constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;               // Q.K^T issuer (and TMEM owner)
-constexpr int PV_WARP0 = 18;               // P_hi . [U_hi; U_lo] issuer
-constexpr int PV_WARP1 = 19;               // P_lo . U_hi issuer
-constexpr int NTHREADS = 20 * 32;
+constexpr int BN = 128;                    // keys per tile (N of Q.K^T, K of P.U)
+constexpr int NEPI_WG = 3;                 // epilogue warpgroups = TMEM S/P buffers
+constexpr int TMA_WARP = 12;
+constexpr int MMA_WARP = 13;               // Q.K^T issuer of even tiles (and TMEM owner); 14: odd tiles
+constexpr int PV_WARP0 = 15;               // P_hi . [U_hi; U_lo] issuer
+constexpr int PV_WARP1 = 16;               // P_lo . U_hi issuer
+constexpr int NTHREADS = 17 * 32;
 constexpr uint32_t BOX_BYTES = 128 * 128;  // query box: 128 rows x 64 16-bit columns
 constexpr uint32_t KBOX_BYTES = BN * 128;  // key box: BN rows x 64 16-bit columns
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int NSB = 4;                     // TMEM S/P buffers of BN columns, one per epilogue warpgroup
+constexpr int NSB = NEPI_WG;               // TMEM S/P buffers of BN columns, one per epilogue warpgroup
 constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 3 RP)
+constexpr int NEPI_WARPS = 4 * NEPI_WG;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 template <int KB, int RP>
@@ -83,8 +85,8 @@ struct Cfg {
     static constexpr int STAGES = K_RAW > 6 ? 6 : (K_RAW < 2 ? 2 : K_RAW);
     static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
     static constexpr uint32_t BAR_OFF = U_OFF + USTAGES * USTAGE_BYTES;
-    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4], pfull[4], ofull, oempty, done[3]
-    static constexpr int NBARS = 2 * STAGES + 2 * USTAGES + 2 + 3 * NSB + 5;
+    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[3], sempty[3], pfull[3], ofull, oempty, done[4]
+    static constexpr int NBARS = 2 * STAGES + 2 * USTAGES + 2 + 3 * NSB + 6;
     static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t SMEM_BYTES = MISC_OFF + 16;
     static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
@@ -194,15 +196,15 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             ptx::mbar_init(&uempty[i], 2);   // both P.U issuers
         }
         ptx::mbar_init(qfull, 1);
-        ptx::mbar_init(qempty, 1);
+        ptx::mbar_init(qempty, 2);          // both Q.K^T issuers
         for (int i = 0; i < NSB; ++i) {
             ptx::mbar_init(&sfull[i], 1);
             ptx::mbar_init(&sempty[i], 2);   // both P.U issuers
             ptx::mbar_init(&pfull[i], 4);   // the 4 warps of the warpgroup owning buffer i
         }
         ptx::mbar_init(ofull, 2);           // both P.U issuers
-        ptx::mbar_init(oempty, 16);         // every epilogue warp reads its share of O
-        for (int i = 0; i < 3; ++i) ptx::mbar_init(&done[i], 1);   // one per MMA issuer
+        ptx::mbar_init(oempty, 8);          // the two warpgroups that read O
+        for (int i = 0; i < 4; ++i) ptx::mbar_init(&done[i], 1);   // one per MMA issuer
         *abort = 0;
         ptx::fence_mbar_init();
     }
@@ -253,9 +255,10 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
             }
         }
-    } else if (warp == MMA_WARP) {
-        // ---- Q.K^T issuer ---------------------------------------------------
+    } else if (warp == MMA_WARP || warp == MMA_WARP + 1) {
+        // ---- Q.K^T issuers: warp MMA_WARP + q takes the tiles m = q (mod 2) ----
         if (lane == 0) {
+            const int q = warp - MMA_WARP;
             const uint32_t q_base = ptx::smem_u32(sQ), k_base = ptx::smem_u32(sK);
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
@@ -269,22 +272,25 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     ++qcount;
                     cur_rt = rt;
                 }
-                if (!FD_WAIT(7, &kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
-                if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
-                ptx::tc_fence_after();
-                const uint32_t ka = k_base + stage * C::STAGE_BYTES;
-                for (int ks = 0; ks < ksteps; ++ks) {
-                    const uint32_t kc = (ks & 3) * 32;
-                    ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + (ks >> 2) * BOX_BYTES + kc),
-                                 ptx::sw128_kmajor_desc(ka + (ks >> 2) * KBOX_BYTES + kc), idesc_qk, ks > 0);
+                if ((int)(m & 1) == q) {
+                    if (!FD_WAIT(7, &kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
+                    if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
+                    ptx::tc_fence_after();
+                    const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                    for (int ks = 0; ks < ksteps; ++ks) {
+                        const uint32_t kc = (ks & 3) * 32;
+                        ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + (ks >> 2) * BOX_BYTES + kc),
+                                     ptx::sw128_kmajor_desc(ka + (ks >> 2) * KBOX_BYTES + kc), idesc_qk, ks > 0);
+                    }
+                    ptx::umma_commit(&sfull[b]);
+                    ptx::umma_commit(&kempty[stage]);
                 }
-                ptx::umma_commit(&sfull[b]);
-                ptx::umma_commit(&kempty[stage]);
+                // both issuers arrive at every row-tile end (qempty counts 2)
                 if ((n + 1 == n1) || (jt + 1 == n_jt)) ptx::umma_commit(qempty);
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
-            ptx::umma_commit(done);
-            FD_WAIT(11, done, 0, abort, status, WAIT_LIMIT_NS);
+            ptx::umma_commit(&done[q]);
+            FD_WAIT(11, &done[q], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else if (warp == PV_WARP0 || warp == PV_WARP1) {
         // ---- P.U issuers: warp PV_WARP0 runs O1 += P_hi [U_hi; U_lo] (N = 2 RP),
@@ -325,12 +331,12 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     ++ocount;
                 }
             }
-            ptx::umma_commit(&done[1 + t]);
-            FD_WAIT(11, &done[1 + t], 0, abort, status, WAIT_LIMIT_NS);
+            ptx::umma_commit(&done[2 + t]);
+            FD_WAIT(11, &done[2 + t], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else {
         // ---- epilogue warpgroups ------------------------------------------
-        const int wg = warp >> 2;             // key quarter of every tile, and O column quarter
+        const int wg = warp >> 2;             // tiles m = wg (mod 3); O column half wg (wg < 2)
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -369,11 +375,11 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&pfull[b]);
             }
-            if (n + 1 == n1 || jt + 1 == n_jt) {
-                // read this warpgroup's quarter of the O columns, scale, store
+            if ((n + 1 == n1 || jt + 1 == n_jt) && wg < 2) {
+                // read this warpgroup's half of the O columns, scale, store
                 if (!FD_WAIT(10, ofull, segs & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
-                constexpr int NC = RP / 4;
+                constexpr int NC = RP / 2;
                 const int c0 = wg * NC;
                 float o[NC], o2[NC], o3[NC];
                 tmem_ld_cols<NC>(t_lane + O_COL + c0, o);             // P_hi U_hi
