@@ -32,7 +32,9 @@ int launch_zero_rows(int64_t nq, int rc, const RowEpilogue& ep, cudaStream_t s) 
 }
 
 static bool valid_dtype(int t) { return t == FD_DTYPE_F32 || t == FD_DTYPE_F16 || t == FD_DTYPE_BF16 || t == FD_DTYPE_F64; }
-static bool valid_tile(int t) { return t == FD_TILE_BF16 || t == FD_TILE_F32 || t == FD_TILE_F16; }
+static bool valid_tile(int t) {
+    return t == FD_TILE_BF16 || t == FD_TILE_F32 || t == FD_TILE_F16 || t == FD_TILE_F16X3;
+}
 
 // columns of V handled per tile-kernel launch
 static int cols_per_launch(int tile, int r) {
@@ -91,7 +93,7 @@ size_t fd_operand_bytes(int64_t n, int d, int tile) {
     if (n < 0 || d < 1) return 0;
     if (tile == FD_TILE_F32)
         return align256(sizeof(float) * (size_t)n * dp_f32(d)) + align256(sizeof(float) * (size_t)n);
-    return align256(2 * (size_t)n * kd_bf16(d));
+    return align256(2 * (size_t)n * kd_tile(tile, d));
 }
 
 int fd_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, void* stream) {
@@ -108,6 +110,7 @@ int fd_pack_operand(const void* X, int dtype, int64_t n, int d, const float* shi
     FD_CHECK_ARG(valid_tile(tile), "bad tile %d", tile);
     FD_CHECK_ARG(side == FD_SIDE_QUERY || side == FD_SIDE_KEY, "bad side %d", side);
     FD_CHECK_ARG(beta > 0.f, "beta must be positive (got %g)", (double)beta);
+    FD_CHECK_ARG(tile != FD_TILE_F16X3 || d <= 66, "FD_TILE_F16X3 supports d <= 66 (got %d)", d);
     FD_CHECK_ARG(n == 0 || (X && operand), "null pointer");
     FD_CHECK_ARG(((uintptr_t)operand & 255) == 0, "operand must be 256-byte aligned");
     return launch_pack(X, dtype, n, d, shift, beta, side, tile, operand, (cudaStream_t)stream);

@@ -62,6 +62,11 @@ __device__ __forceinline__ double load_as_f64(const void* p, int dtype, int64_t 
 // sqrt(beta), dp = round_up(d,4), followed by n fp32 squared norms of the
 // stored values (so the tile kernel evaluates exp(-||a-b||^2)).
 static inline int kd_bf16(int d) { return (int)round_up(d + 6, 16); }
+// FD_TILE_F16X3 operand: query row [a_hi | a_hi | a_lo | 1 1 1 | split3(n)], key row
+// [b_hi | b_lo | b_hi | split3(n) | 1 1 1]: the three products a_hi b_hi +
+// a_hi b_lo + a_lo b_hi carry the fp32 value of a.b to ~2^-22.
+static inline int kd_f16x3(int d) { return (int)round_up(3 * d + 6, 16); }
+static inline int kd_tile(int tile, int d) { return tile == FD_TILE_F16X3 ? kd_f16x3(d) : kd_bf16(d); }
 static inline int dp_f32(int d) { return (int)round_up(d, 4); }
 
 }  // namespace fd

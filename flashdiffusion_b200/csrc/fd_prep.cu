@@ -92,6 +92,54 @@ __global__ void pack16_kernel(const void* __restrict__ X, int dtype, int64_t n, 
     for (int k = d + 6 + lane; k < kd; k += 32) o[k] = F::from(0.0);
 }
 
+// fp32-class operand: every coordinate split into fp16 hi + lo (layout in
+// fd_common.cuh, kd_f16x3); the norm is that of the split point hi + lo.
+__global__ void pack_f16x3_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
+                                  const float* __restrict__ shift, double s, int side, int kd,
+                                  __half* __restrict__ out, int* __restrict__ status) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= n) return;
+    __half* o = out + row * kd;
+    double ss = 0.0, amax = 0.0;
+    for (int k = lane; k < d; k += 32) {
+        double x = load_as_f64(X, dtype, row * d + k);
+        if (shift) x -= (double)shift[k];
+        x *= s;
+        const __half hi = H16::from(x);
+        const __half lo = H16::from(x - H16::to(hi));
+        const double a = H16::to(hi) + H16::to(lo);
+        ss += a * a;
+        amax = fmax(amax, fabs(x));
+        o[k] = hi;
+        if (side == FD_SIDE_QUERY) { o[d + k] = hi; o[2 * d + k] = lo; }
+        else { o[d + k] = lo; o[2 * d + k] = hi; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        amax = fmax(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    }
+    const int e = 3 * d;
+    if (lane == 0) {
+        const double nrm = -0.5 * ss;
+        const __half hi = H16::from(nrm);
+        const double r1 = nrm - H16::to(hi);
+        const __half mid = H16::from(r1);
+        const __half lo = H16::from(r1 - H16::to(mid));
+        if (amax > 0.99 * H16::kMax || -nrm > 0.99 * H16::kMax || !(ss == ss)) atomicExch(status, FD_ERR_RANGE);
+        const __half one = H16::from(1.0);
+        if (side == FD_SIDE_QUERY) {
+            o[e + 0] = one; o[e + 1] = one; o[e + 2] = one;
+            o[e + 3] = hi; o[e + 4] = mid; o[e + 5] = lo;
+        } else {
+            o[e + 0] = hi; o[e + 1] = mid; o[e + 2] = lo;
+            o[e + 3] = one; o[e + 4] = one; o[e + 5] = one;
+        }
+    }
+    for (int k = e + 6 + lane; k < kd; k += 32) o[k] = H16::from(0.0);
+}
+
 // fp32 operand: centred points scaled by sqrt(beta) [n][dp], then n squared
 // norms of the stored values.  One warp per row.
 __global__ void pack_f32_kernel(const void* __restrict__ X, int dtype, int64_t n, int d,
@@ -258,7 +306,13 @@ int launch_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, c
 int launch_pack(const void* X, int dtype, int64_t n, int d, const float* shift, float beta, int side,
                 int tile, void* op, cudaStream_t s) {
     if (n == 0) return FD_OK;
-    if (tile == FD_TILE_BF16 || tile == FD_TILE_F16) {
+    if (tile == FD_TILE_F16X3) {
+        const double sc = sqrt(2.0 * (double)beta * 1.4426950408889634);
+        int* status = nullptr;
+        FD_TRY(status_word(&status));
+        pack_f16x3_kernel<<<grid_for(n, 8), 256, 0, s>>>(X, dtype, n, d, shift, sc, side, kd_f16x3(d), (__half*)op,
+                                                         status);
+    } else if (tile == FD_TILE_BF16 || tile == FD_TILE_F16) {
         const double sc = sqrt(2.0 * (double)beta * 1.4426950408889634);  // sqrt(2 beta log2(e))
         int* status = nullptr;
         FD_TRY(status_word(&status));

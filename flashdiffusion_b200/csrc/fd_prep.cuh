@@ -62,6 +62,8 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
 int read_and_clear_status(cudaStream_t s, int* status);
 // Device address of the library's status word (bounded-wait timeouts, fp16 range).
 int status_word(int** ptr);
-static inline bool is_tc_tile(int tile) { return tile == FD_TILE_BF16 || tile == FD_TILE_F16; }
+static inline bool is_tc_tile(int tile) {
+    return tile == FD_TILE_BF16 || tile == FD_TILE_F16 || tile == FD_TILE_F16X3;
+}
 
 }  // namespace fd

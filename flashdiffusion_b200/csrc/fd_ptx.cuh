@@ -135,6 +135,17 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// K-major descriptors with 32- or 64-byte swizzle (16- or 32-column 16-bit
+// rows), 8-row atoms of 256 / 512 B.
+__device__ __forceinline__ uint64_t sw32_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+}
+__device__ __forceinline__ uint64_t sw64_kmajor_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+
 // Instruction descriptor, kind::f16: A and B of the same 16-bit type (fp16
 // when f16, else bf16), both K-major, fp32 D, shape MxN.
 __host__ __device__ constexpr uint32_t idesc_f32acc(int M, int N, bool f16) {

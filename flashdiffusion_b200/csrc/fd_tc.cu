@@ -45,11 +45,15 @@ constexpr int URING = 4;                    // depth of the right-hand-side ring
 constexpr uint32_t U_BYTES = BN * 4;        // one key tile of u (fp32)
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s per pipeline wait
 
-template <int KB>
+template <int KF, int NW>
 struct Cfg {
-    static constexpr int STAGES = KB == 1 ? 6 : (KB == 2 ? 4 : 2);
-    static constexpr uint32_t Q_BYTES = NSUB * KB * BOX_BYTES;
-    static constexpr uint32_t STAGE_BYTES = KB * BOX_BYTES;
+    using G = Geo<KF, NW>;
+    static constexpr uint32_t SUB_BYTES = G::bytes(BM);        // one query subtile
+    static constexpr uint32_t Q_BYTES = NSUB * SUB_BYTES;
+    static constexpr uint32_t STAGE_BYTES = G::bytes(BN);      // one key tile
+    static constexpr int STAGES_RAW = (int)((220u * 1024u - Q_BYTES - URING * U_BYTES) / STAGE_BYTES);
+    static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+    static_assert(STAGES >= 2, "shared memory budget");
     static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
     static constexpr uint32_t BAR_OFF = U_OFF + URING * U_BYTES;
     // barriers: kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4],
@@ -79,12 +83,14 @@ __device__ __forceinline__ void chunk16_r1(const uint32_t (&v)[16], const float*
     }
 }
 
-template <int KB, int EMU>
+template <int KF, int NW, int EMU>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-          const float* __restrict__ u, int64_t nq, int kd, uint32_t idesc, Sched sc, RowEpilogue ep,
+          const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
+          const float* __restrict__ u, int64_t nq, uint32_t idesc, Sched sc, RowEpilogue ep,
           double* __restrict__ part, int* __restrict__ status) {
-    using C = Cfg<KB>;
+    using C = Cfg<KF, NW>;
+    using G = typename C::G;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = base;
@@ -111,7 +117,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
     const int cta = blockIdx.x;
     const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
     const int64_t n_jt = sc.n_jt;
-    const int ksteps = kd / 16;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::STAGES; ++i) {
@@ -161,18 +166,23 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 if (rt != cur_rt) {
                     if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
-                    for (int s = 0; s < NSUB; ++s)
-                        for (int kb = 0; kb < KB; ++kb)
-                            ptx::tma_load_2d(sQ + (s * KB + kb) * BOX_BYTES, &tmq, qfull, kb * 64,
+                    for (int s = 0; s < NSUB; ++s) {
+                        for (int kb = 0; kb < KF; ++kb)
+                            ptx::tma_load_2d(sQ + s * C::SUB_BYTES + kb * BOX_BYTES, &tmq, qfull, kb * 64,
                                              (int)(rt * ROWS + s * BM));
+                        if (NW) ptx::tma_load_2d(sQ + s * C::SUB_BYTES + KF * BOX_BYTES, &tmq_n, qfull, KF * 64,
+                                                 (int)(rt * ROWS + s * BM));
+                    }
                     cur_rt = rt;
                     ++qcount;
                 }
                 if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
-                for (int kb = 0; kb < KB; ++kb)
-                    ptx::tma_load_2d(sK + (stage * KB + kb) * BOX_BYTES, &tmk, &kfull[stage], kb * 64,
+                for (int kb = 0; kb < KF; ++kb)
+                    ptx::tma_load_2d(sK + stage * C::STAGE_BYTES + kb * BOX_BYTES, &tmk, &kfull[stage], kb * 64,
                                      (int)(jt * BN));
+                if (NW) ptx::tma_load_2d(sK + stage * C::STAGE_BYTES + KF * BOX_BYTES, &tmk_n, &kfull[stage],
+                                         KF * 64, (int)(jt * BN));
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
                 // right-hand side of this key tile into the u ring
                 const int us = (int)(m & (URING - 1));
@@ -207,13 +217,11 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     const int b = s * 2 + p;
                     if (!ptx::wait_bounded(&sempty[b], (use & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::tc_fence_after();
-                    const uint32_t qa = q_base + s * KB * BOX_BYTES;
+                    const uint32_t qa = q_base + s * C::SUB_BYTES;
                     const uint32_t ka = k_base + stage * C::STAGE_BYTES;
-                    for (int ks = 0; ks < ksteps; ++ks) {
-                        const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
-                        ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(qa + off),
-                                     ptx::sw128_kmajor_desc(ka + off), idesc, ks > 0);
-                    }
+#pragma unroll
+                    for (int ks = 0; ks < G::KSTEPS; ++ks)
+                        ptx::umma_ss(tmem + b * BN, G::desc(qa, BM, ks), G::desc(ka, BN, ks), idesc, ks > 0);
                     ptx::umma_commit(&sfull[b]);
                 }
                 ptx::umma_commit(&kempty[stage]);
@@ -355,21 +363,30 @@ static int get_encode(EncodeTiledFn* fn) {
     return FD_OK;
 }
 
-// 2-D bf16 map over a [rows][cols] row-major matrix, 64 x box_rows boxes, 128-byte swizzle.
-int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16) {
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16,
+                  int box_cols) {
     EncodeTiledFn enc;
     FD_TRY(get_encode(&enc));
     FD_CHECK_ARG(((uintptr_t)ptr & 15) == 0, "tile operand must be 16-byte aligned");
     FD_CHECK_ARG((cols * 2) % 16 == 0, "tile operand row pitch must be a multiple of 16 bytes");
+    FD_CHECK_ARG(box_cols == 64 || box_cols == 32 || box_cols == 16, "box width %d", box_cols);
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    const CUtensorMapSwizzle sw = box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : (box_cols == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                     const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return FD_OK;
+}
+
+void split_kd(int kd, int* kf, int* nw) {
+    *kf = kd / 64;
+    *nw = kd % 64;
+    if (*nw == 48) { *kf += 1; *nw = 0; }
 }
 
 int num_sms() {
@@ -383,41 +400,43 @@ size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
     return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS);
 }
 
-template <int KB, int EMU>
-static int launch_tc_kb(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
-                        uint32_t idesc, const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
-    using C = tc::Cfg<KB>;
-    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KB, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+struct TcArgs {
+    CUtensorMap mq, mk, mqn, mkn;
+    const float* u;
+    int64_t nq;
+    uint32_t idesc;
+    tc::Sched sc;
+    RowEpilogue ep;
+    double* part;
+};
+
+template <int KF, int NW, int EMU>
+static int launch_tc_kb(const TcArgs& a, cudaStream_t s) {
+    using C = tc::Cfg<KF, NW>;
+    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tc_kernel<KF, NW, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
     int* status = nullptr;
     FD_TRY(status_word(&status));
-    tc::tc_kernel<KB, EMU><<<sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, u, nq, kd, idesc, sc, ep, part,
-                                                                        status);
+    tc::tc_kernel<KF, NW, EMU><<<a.sc.grid, tc::NTHREADS, C::SMEM_ALLOC, s>>>(a.mq, a.mk, a.mqn, a.mkn, a.u, a.nq,
+                                                                              a.idesc, a.sc, a.ep, a.part, status);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
 
 // Columns per 16 whose exp2 runs on the FMA pipe instead of MUFU.  Default 0;
-// FD_EXP2_FMA_COLS (0, 2, 4 or 6) overrides it for tuning.
+// FD_EXP2_FMA_COLS=2 moves 2 of every 16 onto the polynomial.
 static int exp2_fma_cols() {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("FD_EXP2_FMA_COLS");
-        const int x = e ? atoi(e) : 0;
-        v = (x == 0 || x == 2 || x == 4 || x == 6) ? x : 0;
+        v = (e && atoi(e) == 2) ? 2 : 0;
     }
     return v;
 }
 
-template <int KB>
-static int launch_tc_emu(const CUtensorMap& mq, const CUtensorMap& mk, const float* u, int64_t nq, int kd,
-                         uint32_t idesc, const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
-    switch (exp2_fma_cols()) {
-        case 2: return launch_tc_kb<KB, 2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
-        case 4: return launch_tc_kb<KB, 4>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
-        case 6: return launch_tc_kb<KB, 6>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
-        default: return launch_tc_kb<KB, 0>(mq, mk, u, nq, kd, idesc, sc, ep, part, s);
-    }
+template <int KF, int NW>
+static int launch_tc_emu(const TcArgs& a, cudaStream_t s) {
+    return exp2_fma_cols() == 2 ? launch_tc_kb<KF, NW, 2>(a, s) : launch_tc_kb<KF, NW, 0>(a, s);
 }
 
 int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
@@ -425,28 +444,44 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     if (nq == 0) return FD_OK;
     if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
     if (rc != 1) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path: block right-hand sides not built yet");
-    const int kd = kd_bf16(d);
-    const int kb = (int)cdiv(kd, 64);
-    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path supports d <= 186 (got d=%d)", d);
+    const int kd = kd_tile(tile, d);
+    int kf = 0, nw = 0;
+    split_kd(kd, &kf, &nw);
+    if (kd > 208) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 208)", kd);
     const size_t need = tc_workspace_bytes(nq, nk, rc);
     if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "16-bit tile path: workspace %zu B < %zu B", ws_bytes, need);
-    CUtensorMap mq, mk;
-    const bool f16 = tile == FD_TILE_F16;
-    FD_TRY(make_tile_map(&mq, qop, nq, kd, tc::BM, f16));
-    FD_TRY(make_tile_map(&mk, kop, nk, kd, tc::BN, f16));
-    const uint32_t idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
-    tc::Sched sc;
-    sc.n_jt = cdiv(nk, tc::BN);
-    sc.units = cdiv(nq, tc::ROWS) * sc.n_jt;
-    sc.grid = (int)std::min<int64_t>(num_sms(), sc.units);
-    double* part = (double*)ws;
-    const float* u = (const float*)rhs;
-    switch (kb) {
-        case 1: FD_TRY(launch_tc_emu<1>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
-        case 2: FD_TRY(launch_tc_emu<2>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
-        default: FD_TRY(launch_tc_emu<3>(mq, mk, u, nq, kd, idesc, sc, ep, part, s)); break;
+    TcArgs a;
+    const bool f16 = tile != FD_TILE_BF16;
+    FD_TRY(make_tile_map(&a.mq, qop, nq, kd, tc::BM, f16));
+    FD_TRY(make_tile_map(&a.mk, kop, nk, kd, tc::BN, f16));
+    a.mqn = a.mq;
+    a.mkn = a.mk;
+    if (nw) {
+        FD_TRY(make_tile_map(&a.mqn, qop, nq, kd, tc::BM, f16, nw));
+        FD_TRY(make_tile_map(&a.mkn, kop, nk, kd, tc::BN, f16, nw));
     }
-    tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(part, sc, nq, ep);
+    a.idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
+    a.sc.n_jt = cdiv(nk, tc::BN);
+    a.sc.units = cdiv(nq, tc::ROWS) * a.sc.n_jt;
+    a.sc.grid = (int)std::min<int64_t>(num_sms(), a.sc.units);
+    a.part = (double*)ws;
+    a.u = (const float*)rhs;
+    a.nq = nq;
+    a.ep = ep;
+    switch (kf * 100 + nw) {
+        case 16: FD_TRY((launch_tc_emu<0, 16>(a, s))); break;
+        case 32: FD_TRY((launch_tc_emu<0, 32>(a, s))); break;
+        case 100: FD_TRY((launch_tc_emu<1, 0>(a, s))); break;
+        case 116: FD_TRY((launch_tc_emu<1, 16>(a, s))); break;
+        case 132: FD_TRY((launch_tc_emu<1, 32>(a, s))); break;
+        case 200: FD_TRY((launch_tc_emu<2, 0>(a, s))); break;
+        case 216: FD_TRY((launch_tc_emu<2, 16>(a, s))); break;
+        case 232: FD_TRY((launch_tc_emu<2, 32>(a, s))); break;
+        case 300: FD_TRY((launch_tc_emu<3, 0>(a, s))); break;
+        case 316: FD_TRY((launch_tc_emu<3, 16>(a, s))); break;
+        default: return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: no kernel for kd=%d", kd);
+    }
+    tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(a.part, a.sc, nq, ep);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }

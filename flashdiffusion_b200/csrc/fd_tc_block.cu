@@ -71,13 +71,14 @@ constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) 
 constexpr int NEPI_WARPS = 4 * NEPI_WG;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
-template <int KB, int RP>
+template <int KF, int NW, int RP>
 struct Cfg {
-    static constexpr uint32_t Q_BYTES = KB * BOX_BYTES;
+    using G = tc::Geo<KF, NW>;
+    static constexpr uint32_t Q_BYTES = G::bytes(BM);
     static constexpr uint32_t UT_BOX = RP * 128;                 // RP rows x 64 keys
     // two rings: K tiles (released as soon as Q.K^T is done) and U^T tiles
     // (U_hi^T and U_lo^T, 2 boxes each; released after P.U, i.e. after the epilogue)
-    static constexpr uint32_t STAGE_BYTES = KB * KBOX_BYTES;
+    static constexpr uint32_t STAGE_BYTES = G::bytes(BN);
     static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX;
     static constexpr uint32_t BUDGET = 222u * 1024u - Q_BYTES;
     static constexpr int USTAGES = 4;              // U^T tiles live from their load to their P.U
@@ -149,13 +150,15 @@ __device__ __forceinline__ void exp2_to_f16x2(const uint32_t (&v)[16], uint32_t 
     }
 }
 
-template <int KB, int RP>
+template <int KF, int NW, int RP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
                 const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
-                int64_t nq, int kd, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
+                int64_t nq, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
                 double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2) {
-    using C = Cfg<KB, RP>;
+    using C = Cfg<KF, NW, RP>;
+    using G = typename C::G;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sQ = base;
@@ -181,7 +184,6 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     const int cta = blockIdx.x;
     const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
     const int64_t n_jt = sc.n_jt;
-    const int ksteps = kd / 16;
 #ifdef FD_PROFILE_WAITS
     const long long t_start = clock64();
 #endif
@@ -233,16 +235,18 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 if (rt != cur_rt) {
                     if (qcount > 0 && !FD_WAIT(0, qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
-                    for (int kb = 0; kb < KB; ++kb)
+                    for (int kb = 0; kb < KF; ++kb)
                         ptx::tma_load_2d(sQ + kb * BOX_BYTES, &tmq, qfull, kb * 64, (int)(rt * BM));
+                    if (NW) ptx::tma_load_2d(sQ + KF * BOX_BYTES, &tmq_n, qfull, KF * 64, (int)(rt * BM));
                     cur_rt = rt;
                     ++qcount;
                 }
                 if (!FD_WAIT(1, &kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 uint8_t* st = sK + stage * C::STAGE_BYTES;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
-                for (int kb = 0; kb < KB; ++kb)
+                for (int kb = 0; kb < KF; ++kb)
                     ptx::tma_load_2d(st + kb * KBOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                if (NW) ptx::tma_load_2d(st + KF * KBOX_BYTES, &tmk_n, &kfull[stage], KF * 64, (int)(jt * BN));
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
                 // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
                 if (!FD_WAIT(2, &uempty[ustage], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
@@ -277,11 +281,9 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
                     ptx::tc_fence_after();
                     const uint32_t ka = k_base + stage * C::STAGE_BYTES;
-                    for (int ks = 0; ks < ksteps; ++ks) {
-                        const uint32_t kc = (ks & 3) * 32;
-                        ptx::umma_ss(tmem + b * BN, ptx::sw128_kmajor_desc(q_base + (ks >> 2) * BOX_BYTES + kc),
-                                     ptx::sw128_kmajor_desc(ka + (ks >> 2) * KBOX_BYTES + kc), idesc_qk, ks > 0);
-                    }
+#pragma unroll
+                    for (int ks = 0; ks < G::KSTEPS; ++ks)
+                        ptx::umma_ss(tmem + b * BN, G::desc(q_base, BM, ks), G::desc(ka, BN, ks), idesc_qk, ks > 0);
                     ptx::umma_commit(&sfull[b]);
                     ptx::umma_commit(&kempty[stage]);
                 }
@@ -455,35 +457,38 @@ size_t tc_block_workspace_bytes(int rp) {
     return align256(sizeof(double) * 2 * (size_t)num_sms() * tcb::BM * rp);
 }
 
-template <int KB, int RP>
-static int launch_block_t(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mu, const float* colscale,
-                          int rc, int64_t nq, int kd, uint32_t iqk, uint32_t ipv, const tc::Sched& sc,
-                          const RowEpilogue& ep, double* part, cudaStream_t s) {
-    using C = tcb::Cfg<KB, RP>;
+struct BlockArgs {
+    CUtensorMap mq, mk, mqn, mkn, mu;
+    const float* colscale;
+    int rc;
+    int64_t nq;
+    uint32_t iqk, ipv;
+    tc::Sched sc;
+    RowEpilogue ep;
+    double* part;
+};
+
+template <int KF, int NW, int RP>
+static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
+    using C = tcb::Cfg<KF, NW, RP>;
     int* status = nullptr;
     FD_TRY(status_word(&status));
-    FD_CUDA_TRY(cudaFuncSetAttribute(tcb::tc_block_kernel<KB, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FD_CUDA_TRY(cudaFuncSetAttribute(tcb::tc_block_kernel<KF, NW, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
-    tcb::tc_block_kernel<KB, RP><<<sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(mq, mk, mu, colscale, rc, nq, kd, iqk,
-                                                                               ipv, sc, ep, part, status,
-                                                                               ptx::idesc_f32acc(tcb::BM, 2 * RP, true));
+    tcb::tc_block_kernel<KF, NW, RP><<<a.sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(
+        a.mq, a.mk, a.mqn, a.mkn, a.mu, a.colscale, a.rc, a.nq, a.iqk, a.ipv, a.sc, a.ep, a.part, status,
+        ptx::idesc_f32acc(tcb::BM, 2 * RP, true));
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
 
 // Columns of U per launch: the three accumulator blocks (3 x 32) fit next to
-// the four 96-column S buffers in the 512 TMEM columns.
+// the three 128-column S buffers in the 512 TMEM columns.
 int block_max_cols(int d) { (void)d; return 32; }
 
-template <int KB>
-static int launch_block_kb(int rp, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mu,
-                           const float* colscale, int rc, int64_t nq, int kd, uint32_t iqk, uint32_t ipv,
-                           const tc::Sched& sc, const RowEpilogue& ep, double* part, cudaStream_t s) {
-    switch (rp) {
-        case 16: return launch_block_t<KB, 16>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
-        case 32: return launch_block_t<KB, 32>(mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s);
-        default: return set_error(FD_ERR_UNSUPPORTED, "block tile path: at most 32 columns per launch");
-    }
+template <int KF, int NW>
+static int launch_block_kb(int rp, const BlockArgs& a, cudaStream_t s) {
+    return rp == 16 ? launch_block_t<KF, NW, 16>(a, s) : launch_block_t<KF, NW, 32>(a, s);
 }
 
 // ut: [2 rp][ld] fp16 transposed, column-scaled right-hand side (hi rows, then
@@ -495,30 +500,48 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
     FD_CHECK_ARG(rc >= 1 && rc <= 32, "block tile path: %d columns per launch (max 32)", rc);
     const int rp = block_rp(rc);
-    const int kd = kd_bf16(d);
-    const int kb = (int)cdiv(kd, 64);
-    if (kb > 3) return set_error(FD_ERR_UNSUPPORTED, "16-bit tile path supports d <= 186 (got d=%d)", d);
+    const int kd = kd_tile(tile, d);
+    int kf = 0, nw = 0;
+    split_kd(kd, &kf, &nw);
+    if (kd > 208) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 208)", kd);
     const size_t need = tc_block_workspace_bytes(rp);
     if (ws_bytes < need)
         return set_error(FD_ERR_WORKSPACE, "block tile path: workspace %zu B < %zu B", ws_bytes, need);
-    const bool f16 = tile == FD_TILE_F16;
-    CUtensorMap mq, mk, mu;
-    FD_TRY(make_tile_map(&mq, qop, nq, kd, tcb::BM, f16));
-    FD_TRY(make_tile_map(&mk, kop, nk, kd, tcb::BN, f16));
-    FD_TRY(make_tile_map(&mu, ut, 2 * rp, ld, rp, true));   // U_hi^T rows then U_lo^T rows
-    const uint32_t iqk = ptx::idesc_f32acc(tcb::BM, tcb::BN, f16);
-    const uint32_t ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
-    tc::Sched sc;
-    sc.n_jt = cdiv(nk, tcb::BN);
-    sc.units = cdiv(nq, tcb::BM) * sc.n_jt;
-    sc.grid = (int)std::min<int64_t>(num_sms(), sc.units);
-    double* part = (double*)ws;
-    switch (kb) {
-        case 1: FD_TRY(launch_block_kb<1>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
-        case 2: FD_TRY(launch_block_kb<2>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
-        default: FD_TRY(launch_block_kb<3>(rp, mq, mk, mu, colscale, rc, nq, kd, iqk, ipv, sc, ep, part, s)); break;
+    const bool f16 = tile != FD_TILE_BF16;
+    BlockArgs a;
+    FD_TRY(make_tile_map(&a.mq, qop, nq, kd, tcb::BM, f16));
+    FD_TRY(make_tile_map(&a.mk, kop, nk, kd, tcb::BN, f16));
+    a.mqn = a.mq;
+    a.mkn = a.mk;
+    if (nw) {
+        FD_TRY(make_tile_map(&a.mqn, qop, nq, kd, tcb::BM, f16, nw));
+        FD_TRY(make_tile_map(&a.mkn, kop, nk, kd, tcb::BN, f16, nw));
     }
-    tcb::tc_block_fixup_kernel<<<(unsigned)cdiv(nq, tcb::BM), 256, 0, s>>>(part, sc, nq, rc, rp, ep);
+    FD_TRY(make_tile_map(&a.mu, ut, 2 * rp, ld, rp, true));   // U_hi^T rows then U_lo^T rows
+    a.iqk = ptx::idesc_f32acc(tcb::BM, tcb::BN, f16);
+    a.ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
+    a.sc.n_jt = cdiv(nk, tcb::BN);
+    a.sc.units = cdiv(nq, tcb::BM) * a.sc.n_jt;
+    a.sc.grid = (int)std::min<int64_t>(num_sms(), a.sc.units);
+    a.part = (double*)ws;
+    a.colscale = colscale;
+    a.rc = rc;
+    a.nq = nq;
+    a.ep = ep;
+    switch (kf * 100 + nw) {
+        case 16: FD_TRY((launch_block_kb<0, 16>(rp, a, s))); break;
+        case 32: FD_TRY((launch_block_kb<0, 32>(rp, a, s))); break;
+        case 100: FD_TRY((launch_block_kb<1, 0>(rp, a, s))); break;
+        case 116: FD_TRY((launch_block_kb<1, 16>(rp, a, s))); break;
+        case 132: FD_TRY((launch_block_kb<1, 32>(rp, a, s))); break;
+        case 200: FD_TRY((launch_block_kb<2, 0>(rp, a, s))); break;
+        case 216: FD_TRY((launch_block_kb<2, 16>(rp, a, s))); break;
+        case 232: FD_TRY((launch_block_kb<2, 32>(rp, a, s))); break;
+        case 300: FD_TRY((launch_block_kb<3, 0>(rp, a, s))); break;
+        case 316: FD_TRY((launch_block_kb<3, 16>(rp, a, s))); break;
+        default: return set_error(FD_ERR_UNSUPPORTED, "block tile path: no kernel for kd=%d", kd);
+    }
+    tcb::tc_block_fixup_kernel<<<(unsigned)cdiv(nq, tcb::BM), 256, 0, s>>>(a.part, a.sc, nq, rc, rp, ep);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }

@@ -7,6 +7,22 @@
 namespace fd {
 namespace tc {
 
+// Column geometry of a tile operand in shared memory: KF full boxes of 64
+// columns (128-byte rows, 128-byte swizzle), then an optional narrow box of
+// NW in {0, 16, 32} columns (32- / 64-byte swizzle), so a row of kd = 64 KF + NW
+// columns is stored without padding it to a multiple of 64.
+template <int KF, int NW>
+struct Geo {
+    static constexpr int KSTEPS = KF * 4 + NW / 16;
+    static constexpr uint32_t bytes(int rows) { return (uint32_t)rows * (KF * 128 + NW * 2); }
+    // shared-memory descriptor of 16-column k-step ks of a tile of `rows` rows at saddr
+    __device__ static __forceinline__ uint64_t desc(uint32_t saddr, int rows, int ks) {
+        if (ks < KF * 4) return ptx::sw128_kmajor_desc(saddr + (ks >> 2) * rows * 128 + (ks & 3) * 32);
+        const uint32_t nb = saddr + KF * rows * 128 + (ks - KF * 4) * 32;
+        return NW == 32 ? ptx::sw64_kmajor_desc(nb) : ptx::sw32_kmajor_desc(nb);
+    }
+};
+
 struct Sched {
     int64_t n_jt;    // key tiles per row tile
     int64_t units;   // n_rt * n_jt
@@ -48,7 +64,12 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {
 }  // namespace tc
 
 // Host helpers defined in fd_tc.cu.
-int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16);
+// 2-D map over a [rows][cols] 16-bit row-major matrix, box_cols x box_rows boxes
+// with the swizzle that matches box_cols (64 -> 128 B, 32 -> 64 B, 16 -> 32 B).
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16,
+                  int box_cols = 64);
+// kd = 64 kf + nw with nw in {0, 16, 32} (a remainder of 48 takes a full box).
+void split_kd(int kd, int* kf, int* nw);
 int num_sms();
 
 }  // namespace fd

@@ -37,8 +37,8 @@ class DiffusionMap:
 
     def __init__(self, beta: float = 1.0, alpha: float = 0.5, n_components: int = 8, tile: int = 512,
                  precision: str = "ramp", verbose: bool = False):
-        if precision not in ("ramp", "f16", "bf16", "fp32"):
-            raise ValueError(f"precision must be 'ramp', 'f16', 'bf16' or 'fp32' (got {precision!r})")
+        if precision not in ("ramp", "f16", "bf16", "fp32", "f16x3"):
+            raise ValueError(f"precision must be 'ramp', 'f16', 'bf16', 'fp32' or 'f16x3' (got {precision!r})")
         self.beta = beta
         self.alpha = alpha
         self.n_components = n_components
@@ -78,7 +78,7 @@ class DiffusionMap:
         self._Xd = to_device(X, torch.float32)
         first = "f16" if self.precision == "ramp" else self.precision
         self._cuda_state = self._state(first)
-        self._hi_state = self._cuda_state if self.precision == "fp32" else None
+        self._hi_state = self._cuda_state if self.precision in ("fp32", "f16x3") else None
         self.timings_["fit_s"] = self._cuda_state.timings["precompute_s"]
         self._mirror(self._cuda_state)
         if self.verbose:
@@ -111,7 +111,8 @@ class DiffusionMap:
         t0 = time.perf_counter()
         if self.precision == "ramp":
             def hi():
-                self._hi_state = self._state("fp32")
+                # fp32-class tensor-core tiles (split operands) when d <= 66, else fp32 SIMT tiles
+                self._hi_state = self._state("f16x3")
                 return self._hi_state
             vals, vecs, info = ramp_eigsh(self._cuda_state, hi, N, k, tol=tol,
                                           maxiter=maxiter if maxiter else 1000)

@@ -76,9 +76,9 @@ def trlan(op: Callable[[torch.Tensor], torch.Tensor], N: int, k: int, tol: float
     """Thick-restart Lanczos for the k eigenvalues of largest magnitude.
 
     Returns (theta (k,) fp64 host, Y (N,k) fp64 device, residual norms (k,)).
-    Convergence: ||A y - theta y|| <= tol * |theta| for all k pairs, or no
-    progress of the largest relative residual for ``stall_restarts`` restarts
-    (the matvec's own rounding floor).
+    Convergence: ||A y - theta y|| <= tol * |theta| for all k pairs, or no 10 %
+    improvement of the largest relative residual for ``stall_restarts``
+    consecutive restarts (the matvec's own rounding floor).
     """
     m = max(min(ncv, N), k + 1)
     V = torch.zeros((m + 1, N), dtype=torch.float64, device=device)
@@ -122,7 +122,7 @@ def trlan(op: Callable[[torch.Tensor], torch.Tensor], N: int, k: int, tol: float
         if worst <= tol:
             info.converged = True
             break
-        if worst < 0.5 * best:
+        if worst < 0.9 * best:
             best, stall = worst, 0
         else:
             stall += 1
@@ -187,18 +187,18 @@ def ramp_eigsh(op_lo, op_hi_factory, N: int, k: int, tol: float = 0.0, ncv: Opti
     _, y1, _ = trlan(_device_op(op_lo, device), N, k, lo_tol, maxiter, ncv, v0d, device, i1, stall_restarts=2)
     torch.cuda.synchronize(device)
     t1 = time.perf_counter()
-    info.stages.append({"precision": "bf16", "n_matvec": i1.n_matvec, "seconds": t1 - t0,
-                        "max_rel_residual": float(np.max(i1.residuals / 1.0))})
+    info.stages.append({"precision": "16-bit", "n_matvec": i1.n_matvec, "seconds": t1 - t0})
     op_hi = op_hi_factory()
     torch.cuda.synchronize(device)
     t2 = time.perf_counter()
     i2 = SolveInfo()
     start = y1.sum(dim=1)
-    theta, vecs, res = trlan(_device_op(op_hi, device), N, k, tol if tol > 0 else 1e-10, maxiter, ncv, start,
-                             device, i2, stall_restarts=3)
+    theta, vecs, res = trlan(_device_op(op_hi, device), N, k, tol if tol > 0 else 1e-9, maxiter, ncv, start,
+                             device, i2, stall_restarts=4)
     torch.cuda.synchronize(device)
     t3 = time.perf_counter()
-    info.stages.append({"precision": "fp32", "n_matvec": i2.n_matvec, "seconds": t3 - t2,
+    info.stages.append({"precision": getattr(getattr(op_hi, "op", None), "precision", "fp32"),
+                        "n_matvec": i2.n_matvec, "seconds": t3 - t2,
                         "setup_seconds": t2 - t1, "max_rel_residual": float(np.max(res / np.abs(theta)))})
     info.n_matvec = i1.n_matvec + i2.n_matvec
     info.residuals = res

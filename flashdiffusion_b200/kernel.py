@@ -36,7 +36,8 @@ from . import native
 # SM -> kernel family.  This build ships the B200 family only.
 _SM_BACKEND = {100: "sm100", 103: "sm100"}
 
-TILE_NAMES = {"f16": native.TILE_F16, "bf16": native.TILE_BF16, "fp32": native.TILE_F32}
+TILE_NAMES = {"f16": native.TILE_F16, "bf16": native.TILE_BF16, "fp32": native.TILE_F32,
+              "f16x3": native.TILE_F16X3}
 
 
 def _cuda_sm() -> Optional[int]:
@@ -118,7 +119,9 @@ class GaussianOperator:
         self.nq, self.d = Qd.shape
         self.nk = Kd.shape[0]
         self.shift = native.mean_rows(Kd) if shift is None else shift
-        if self.tile == native.TILE_F16:
+        if self.tile == native.TILE_F16X3 and self.d > 66:
+            self.tile, self.precision = native.TILE_F32, "fp32"     # split operand rows would not fit
+        if self.tile in (native.TILE_F16, native.TILE_F16X3):
             # fp16 operands unless some packed value would leave the fp16 range
             native.check_status(self.device)
             self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)
@@ -128,8 +131,11 @@ class GaussianOperator:
             except native.FDError as e:
                 if e.code != native.FD_ERR_RANGE:
                     raise
-                self.tile, self.precision = native.TILE_BF16, "bf16"
-        if self.tile != native.TILE_F16:
+                if self.tile == native.TILE_F16X3:
+                    self.tile, self.precision = native.TILE_F32, "fp32"
+                else:
+                    self.tile, self.precision = native.TILE_BF16, "bf16"
+        if self.tile not in (native.TILE_F16, native.TILE_F16X3):
             self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)
             self.kop = native.pack(Kd, self.beta, native.SIDE_KEY, self.tile, self.shift)
         self.symmetric = K is None

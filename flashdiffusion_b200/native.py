@@ -19,7 +19,7 @@ LIB_PATH = os.path.join(PKG, "libfd_sm100.so")
 
 FD_OK, FD_ERR_ARG, FD_ERR_CUDA, FD_ERR_UNSUPPORTED, FD_ERR_TIMEOUT, FD_ERR_WORKSPACE, FD_ERR_RANGE = range(7)
 DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_F64 = range(4)
-TILE_BF16, TILE_F32, TILE_F16 = 0, 1, 2
+TILE_BF16, TILE_F32, TILE_F16, TILE_F16X3 = 0, 1, 2, 3
 SIDE_QUERY, SIDE_KEY = 0, 1
 
 _TORCH_DTYPE = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16,

@@ -18,7 +18,7 @@ from oracle import fd_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"f16": 2e-3, "bf16": 1e-2, "fp32": 1e-5}
+TOL = {"f16": 2e-3, "bf16": 1e-2, "fp32": 1e-5, "f16x3": 1e-5}
 
 
 def rel_l2(a, b):
@@ -60,7 +60,7 @@ def test_prepass_golden(gold, prec):
         np.testing.assert_allclose(prepass_rowsum(X, X, 1.0, precision=prec), g["D64"], rtol=1e-5)
 
 
-@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32", "f16x3"])
 @pytest.mark.parametrize("n", [0, 1, 2])
 def test_dmap_matvec_golden(gold, prec, n):
     from flashdiffusion_b200 import FlashDiffusion
@@ -69,7 +69,7 @@ def test_dmap_matvec_golden(gold, prec, n):
     rs = g[f"rscale{n}"]
     out = FlashDiffusion(g["X"], g["X"], g["v"][:, None], beta, rscale_q=rs, rscale_k=rs, precision=prec).ravel()
     assert rel_l2(out, g[f"out{n}"]) <= TOL[prec]
-    if prec == "fp32":   # reference test tolerance (tests/test_kernel.py:42-51)
+    if prec in ("fp32", "f16x3"):   # reference test tolerance (tests/test_kernel.py:42-51)
         np.testing.assert_allclose(out, g[f"out{n}"], rtol=2e-4, atol=1e-10)
 
 
@@ -116,7 +116,7 @@ def test_fit_golden_fp32(gold):
     np.testing.assert_allclose(dm.rscale_, g["rscale"], rtol=1e-5)
 
 
-@pytest.mark.parametrize("prec", ["ramp", "fp32"])
+@pytest.mark.parametrize("prec", ["ramp", "fp32", "f16x3"])
 def test_eigenvalues_golden(gold, prec):
     from flashdiffusion_b200 import DiffusionMap
     g = gold("eig.npz")
@@ -149,7 +149,7 @@ def test_nystrom_golden(gold):
     assert rel_l2(c, g["coords"]) <= 1e-5
 
 
-@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32"])
+@pytest.mark.parametrize("prec", ["f16", "bf16", "fp32", "f16x3"])
 @pytest.mark.parametrize("nq,nk,d,r", [(1, 1, 3, 1), (129, 257, 3, 1), (300, 200, 64, 1), (257, 511, 66, 1),
                                        (200, 1000, 128, 1), (130, 700, 186, 1), (70, 90, 5, 4),
                                        (513, 300, 64, 2)])
@@ -271,3 +271,15 @@ def test_block_rhs_smooth_eigvec_like_block():
     rows = np.random.default_rng(0).choice(X.shape[0], 300, replace=False)
     ref = O.flash_diffusion(X[rows], X, V, beta)
     assert rel_l2(out[rows], ref) <= TOL["f16"]
+
+
+def test_f16x3_tensor_core_fp32_class_at_c2_shape():
+    """fp32-class tensor-core tiles at the configuration-2 shape: rows vs the exact fp64 sum."""
+    from flashdiffusion_b200 import synthetic, GaussianOperator
+    X, beta = synthetic.gaussian_mixture(n=60_000, d=64, seed=4)
+    op = GaussianOperator(X, None, beta, "f16x3")
+    assert op.precision == "f16x3"
+    v = np.random.default_rng(5).standard_normal(X.shape[0])
+    out = op.apply(torch.from_numpy(v).cuda(), out_dtype=torch.float64)[:, 0].cpu().numpy()
+    rows = np.random.default_rng(6).choice(X.shape[0], 200, replace=False)
+    assert rel_l2(out[rows], exact_apply(X[rows], X, v[:, None], beta)[:, 0]) <= 1e-5
