@@ -295,7 +295,7 @@ int launch_mean_rows(const void* X, int dtype, int64_t n, int d, float* shift, c
         FD_CUDA_TRY(cudaMemsetAsync(shift, 0, sizeof(float) * d, s));
         return FD_OK;
     }
-    const int64_t cap = 65536;
+    const int64_t cap = 4096;
     const int64_t stride = n > cap ? n / cap : 1;
     const int64_t cnt = n > cap ? cap : n;
     mean_rows_kernel<<<1, 256, 0, s>>>(X, dtype, n, d, stride, cnt, shift);
