@@ -143,6 +143,12 @@ class ClockSampler:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes per launch of the dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum; the capture commands are in
+# the named profile summaries).
+TRAFFIC = {"c2": (70.3e6, "profiles/tc_kernel_c2_dmap_matvec.md")}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -313,7 +319,10 @@ def run_ours(args):
                    "mode": cfg["mode"], "tiles": "f16 tcgen05", "parallelism": f"row-shard x{world}, NCCL all-gather",
                    "l2": "flushed between steps (256 MB write)"},
         "roofline": {"bound": "mufu" if mufu_peak <= tensor_peak_evals else "tensor", "achieved": kern_evals,
-                     "peak": peak_evals, "unit": "evals/s", "frac": kern_evals / peak_evals, "traffic": None,
+                     "peak": peak_evals, "unit": "evals/s", "frac": kern_evals / peak_evals,
+                     "traffic": TRAFFIC[args.config][0] if (args.config in TRAFFIC and not args.n and world == 1) else None,
+                     "traffic_source": TRAFFIC.get(args.config, (None, None))[1],
+                     "algorithmic_bytes_per_launch": 2 * (nq + nk) * (((d + 6 + 15) // 16) * 16) + 8 * (nk * r + nq * r),
                      "peak_basis": "min(MUFU ex2 16/clk/SM x 148 SMs x %.0f MHz, measured bf16 %.0f TFLOP/s / %d flop per eval)"
                                    % (sm_max, bf16_tf, flops_per_eval),
                      "tensor": {"achieved": kern_evals * flops_per_eval / 1e12, "peak": bf16_tf, "unit": "TFLOP/s",

@@ -423,20 +423,28 @@ static int launch_tc_kb(const TcArgs& a, cudaStream_t s) {
     return FD_OK;
 }
 
-// Columns per 16 whose exp2 runs on the FMA pipe instead of MUFU.  Default 0;
-// FD_EXP2_FMA_COLS=2 moves 2 of every 16 onto the polynomial.
-static int exp2_fma_cols() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("FD_EXP2_FMA_COLS");
-        v = (e && atoi(e) == 2) ? 2 : 0;
+// Columns per 16 whose exp2 runs on the FMA pipe instead of MUFU (degree-4
+// polynomial, relative error 3.6e-6): 4 by default for the 16-bit tiles, where
+// MUFU is the limit; 0 for the fp32-class tiles (their error budget is 1e-5).
+// FD_EXP2_FMA_COLS (0, 2, 4, 6 or 8) overrides it.
+static int exp2_fma_cols(int tile) {
+    const char* e = getenv("FD_EXP2_FMA_COLS");
+    if (e) {
+        const int x = atoi(e);
+        return (x == 2 || x == 4 || x == 6 || x == 8) ? x : 0;
     }
-    return v;
+    return tile == FD_TILE_F16X3 ? 0 : 4;
 }
 
 template <int KF, int NW>
-static int launch_tc_emu(const TcArgs& a, cudaStream_t s) {
-    return exp2_fma_cols() == 2 ? launch_tc_kb<KF, NW, 2>(a, s) : launch_tc_kb<KF, NW, 0>(a, s);
+static int launch_tc_emu(const TcArgs& a, int emu, cudaStream_t s) {
+    switch (emu) {
+        case 2: return launch_tc_kb<KF, NW, 2>(a, s);
+        case 4: return launch_tc_kb<KF, NW, 4>(a, s);
+        case 6: return launch_tc_kb<KF, NW, 6>(a, s);
+        case 8: return launch_tc_kb<KF, NW, 8>(a, s);
+        default: return launch_tc_kb<KF, NW, 0>(a, s);
+    }
 }
 
 int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
@@ -468,17 +476,18 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     a.u = (const float*)rhs;
     a.nq = nq;
     a.ep = ep;
+    const int emu = exp2_fma_cols(tile);
     switch (kf * 100 + nw) {
-        case 16: FD_TRY((launch_tc_emu<0, 16>(a, s))); break;
-        case 32: FD_TRY((launch_tc_emu<0, 32>(a, s))); break;
-        case 100: FD_TRY((launch_tc_emu<1, 0>(a, s))); break;
-        case 116: FD_TRY((launch_tc_emu<1, 16>(a, s))); break;
-        case 132: FD_TRY((launch_tc_emu<1, 32>(a, s))); break;
-        case 200: FD_TRY((launch_tc_emu<2, 0>(a, s))); break;
-        case 216: FD_TRY((launch_tc_emu<2, 16>(a, s))); break;
-        case 232: FD_TRY((launch_tc_emu<2, 32>(a, s))); break;
-        case 300: FD_TRY((launch_tc_emu<3, 0>(a, s))); break;
-        case 316: FD_TRY((launch_tc_emu<3, 16>(a, s))); break;
+        case 16: FD_TRY((launch_tc_emu<0, 16>(a, emu, s))); break;
+        case 32: FD_TRY((launch_tc_emu<0, 32>(a, emu, s))); break;
+        case 100: FD_TRY((launch_tc_emu<1, 0>(a, emu, s))); break;
+        case 116: FD_TRY((launch_tc_emu<1, 16>(a, emu, s))); break;
+        case 132: FD_TRY((launch_tc_emu<1, 32>(a, emu, s))); break;
+        case 200: FD_TRY((launch_tc_emu<2, 0>(a, emu, s))); break;
+        case 216: FD_TRY((launch_tc_emu<2, 16>(a, emu, s))); break;
+        case 232: FD_TRY((launch_tc_emu<2, 32>(a, emu, s))); break;
+        case 300: FD_TRY((launch_tc_emu<3, 0>(a, emu, s))); break;
+        case 316: FD_TRY((launch_tc_emu<3, 16>(a, emu, s))); break;
         default: return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: no kernel for kd=%d", kd);
     }
     tc::tc_fixup_kernel<<<(unsigned)cdiv(nq, tc::ROWS), 256, 0, s>>>(a.part, a.sc, nq, ep);
