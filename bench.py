@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--no-lanczos", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU sample (0 = auto)")
     p.add_argument("--n", type=int, default=0, help="override the number of points (small profiling cases)")
+    p.add_argument("--lobpcg", action="store_true", help="block configurations: time LOBPCG to k = r eigenpairs")
+    p.add_argument("--lobpcg-tol", type=float, default=1e-3)
     a = p.parse_args()
     if a.n:
         for c in CONFIGS.values():
@@ -279,19 +281,40 @@ def run_ours(args):
     # their rounding floor, then fp32-class tiles with an fp64 Rayleigh-Ritz),
     # device fp64 basis, outside the timed region
     lanczos = None
-    if not args.no_lanczos and cfg["mode"] == "dmap" and r == 1:
+    if not args.no_lanczos and cfg["mode"] in ("dmap", "doob") and r == 1:
         from flashdiffusion_b200.eigensolver import ramp_eigsh
-        kk = 16
+        # configuration 2: k = 16 of the DMAP operator; configuration 4: k = 8 of the
+        # Doob operator, through its symmetric similar form
+        kk = 16 if cfg["mode"] == "dmap" else 8
+        emode = "dmap" if cfg["mode"] == "dmap" else "doob_sym"
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        vals, _, info = ramp_eigsh(op, lambda: ShardedOperator(Qd, Kd, beta, 0.5, "f16x3", mode="dmap").fit(),
+        lo = op if emode == "dmap" else ShardedOperator(Qd, Kd, beta, 0.5, "f16", mode=emode, h=hd).fit()
+        vals, _, info = ramp_eigsh(lo, lambda: ShardedOperator(Qd, Kd, beta, 0.5, "f16x3", mode=emode, h=hd).fit(),
                                    nq, kk, tol=1e-7)
         torch.cuda.synchronize()
         lt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(lt, op=dist.ReduceOp.MAX)
-        lanczos = {"k": kk, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tol": 1e-7,
+        lanczos = {"k": kk, "operator": emode, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tol": 1e-7,
                    "stages": info.stages, "max_rel_residual": info.stages[-1]["max_rel_residual"],
+                   "top_eigenvalues": [float(x) for x in vals[:4]]}
+
+    # configuration 5: k = 32 eigenpairs by LOBPCG whose block products are single
+    # r = 32 passes of the tensor-core block kernel (16-bit tiles)
+    if not args.no_lanczos and r > 1 and args.lobpcg:
+        from flashdiffusion_b200.eigensolver import SolveInfo, lobpcg_core
+        info = SolveInfo()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        vals, _ = lobpcg_core(lambda B: op.matvec_device(B), nq, r, args.lobpcg_tol, 200, 42, dev, info, guard=16)
+        torch.cuda.synchronize()
+        lt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(lt, op=dist.ReduceOp.MAX)
+        lanczos = {"k": r, "method": "LOBPCG (16 guard columns), 16-bit block tiles", "seconds": float(lt.item()),
+                   "block_columns_applied": info.n_matvec, "iterations": info.n_restart, "tol": args.lobpcg_tol,
+                   "converged": info.converged, "max_rel_residual": float(np.max(info.residuals)),
                    "top_eigenvalues": [float(x) for x in vals[:4]]}
 
     if rank != 0:

@@ -69,6 +69,12 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSB = NEPI_WG;               // TMEM S/P buffers of BN columns, one per epilogue warpgroup
 constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 3 RP)
 constexpr int NEPI_WARPS = 4 * NEPI_WG;
+// O is restarted every `ogroup` key tiles and the group sums are added on the
+// CUDA cores in fp32 (round to nearest): the tensor-core accumulation rounds
+// toward zero, so one TMEM accumulator summed over thousands of P.U products
+// drifts low (measured: a relative bias of 1.7e-3 after 2,048 key tiles,
+// linear in the number of accumulation steps).  With groups of g tiles the
+// bias is about 7.5e-7 g, independent of the number of keys.
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
 
 template <int KF, int NW, int RP>
@@ -156,7 +162,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
                 const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
                 int64_t nq, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
-                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2) {
+                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2, int ogroup) {
     using C = Cfg<KF, NW, RP>;
     using G = typename C::G;
     extern __shared__ uint8_t smem_raw[];
@@ -307,6 +313,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             int ustage = 0;
             uint32_t uph = 0, ocount = 0;
             bool fresh = true;
+            int gcnt = 0;
             int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
             for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
                 const int64_t m = n - n0;
@@ -327,10 +334,12 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 ptx::umma_commit(&sempty[pb]);
                 ptx::umma_commit(&uempty[ustage]);
                 if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
-                if ((n + 1 == n1) || (jt + 1 == n_jt)) {
+                const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
+                if (seg_last || ++gcnt == ogroup) {     // end of an O group
                     ptx::umma_commit(ofull);
                     fresh = true;
                     ++ocount;
+                    gcnt = 0;
                 }
             }
             ptx::umma_commit(&done[2 + t]);
@@ -343,7 +352,12 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
         const int64_t first_rt = n0 / n_jt;
-        uint32_t segs = 0;
+        uint32_t ogroups = 0;
+        int gcnt = 0;
+        constexpr int NC = RP / 2;
+        float oacc[NC];
+#pragma unroll
+        for (int i = 0; i < NC; ++i) oacc[i] = 0.f;
         bool alive = true;
         int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
         for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
@@ -377,21 +391,30 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&pfull[b]);
             }
-            if ((n + 1 == n1 || jt + 1 == n_jt) && wg < 2) {
-                // read this warpgroup's half of the O columns, scale, store
-                if (!FD_WAIT(10, ofull, segs & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+            const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
+            const bool grp_end = seg_last || (++gcnt == ogroup);
+            if (grp_end) gcnt = 0;
+            if (grp_end && wg < 2) {
+                // add this warpgroup's half of the O columns of the finished group
+                if (!FD_WAIT(10, ofull, ogroups & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ++ogroups;
                 ptx::tc_fence_after();
-                constexpr int NC = RP / 2;
                 const int c0 = wg * NC;
                 float o[NC], o2[NC], o3[NC];
                 tmem_ld_cols<NC>(t_lane + O_COL + c0, o);             // P_hi U_hi
                 tmem_ld_cols<NC>(t_lane + O_COL + RP + c0, o2);       // P_hi U_lo
                 tmem_ld_cols<NC>(t_lane + O_COL + 2 * RP + c0, o3);   // P_lo U_hi
-#pragma unroll
-                for (int i = 0; i < NC; ++i) o[i] += o2[i] + o3[i];
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(oempty);
+#pragma unroll
+                for (int i = 0; i < NC; ++i) oacc[i] += o[i] + (o2[i] + o3[i]);
+            }
+            if (seg_last && wg < 2) {
+                const int c0 = wg * NC;
+                float o[NC];
+#pragma unroll
+                for (int i = 0; i < NC; ++i) { o[i] = oacc[i]; oacc[i] = 0.f; }
                 const int64_t gi = rt * BM + row;
                 const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
                 const bool full = seg_first == 0 && jt == n_jt - 1;
@@ -405,7 +428,6 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                         else part[(((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * BM + row) * RP + c] = val;
                     }
                 }
-                ++segs;
             }
         }
         ptx::tc_fence_before();
@@ -466,6 +488,7 @@ struct BlockArgs {
     tc::Sched sc;
     RowEpilogue ep;
     double* part;
+    int ogroup;
 };
 
 template <int KF, int NW, int RP>
@@ -477,7 +500,7 @@ static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
                                      (int)C::SMEM_ALLOC));
     tcb::tc_block_kernel<KF, NW, RP><<<a.sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(
         a.mq, a.mk, a.mqn, a.mkn, a.mu, a.colscale, a.rc, a.nq, a.iqk, a.ipv, a.sc, a.ep, a.part, status,
-        ptx::idesc_f32acc(tcb::BM, 2 * RP, true));
+        ptx::idesc_f32acc(tcb::BM, 2 * RP, true), a.ogroup);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
@@ -485,6 +508,17 @@ static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
 // Columns of U per launch: the three accumulator blocks (3 x 32) fit next to
 // the three 128-column S buffers in the 512 TMEM columns.
 int block_max_cols(int d) { (void)d; return 32; }
+
+// Key tiles per O accumulation group: 8 for the 16-bit tiles (bias 6e-6 against
+// their 2e-3 error budget), 1 for the fp32-class tiles (bias 7e-7).
+// FD_BLOCK_OGROUP (1 to 64) overrides it.
+static int block_ogroup(int tile) {
+    if (const char* e = getenv("FD_BLOCK_OGROUP")) {
+        const int g = atoi(e);
+        if (g >= 1 && g <= 64) return g;
+    }
+    return tile == FD_TILE_F16X3 ? 1 : 8;
+}
 
 template <int KF, int NW>
 static int launch_block_kb(int rp, const BlockArgs& a, cudaStream_t s) {
@@ -528,6 +562,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     a.rc = rc;
     a.nq = nq;
     a.ep = ep;
+    a.ogroup = block_ogroup(tile);
     switch (kf * 100 + nw) {
         case 16: FD_TRY((launch_block_kb<0, 16>(rp, a, s))); break;
         case 32: FD_TRY((launch_block_kb<0, 32>(rp, a, s))); break;

@@ -122,7 +122,10 @@ class ShardedOperator:
     mode "amap": Q != K, rscale_k from the DMAP normalisation of K and the
                  query scale of the reference's only Q != K normaliser
                  (``FD/utils.py:92-102``);
-    mode "doob": DMAP with h: M_h v = M (h v) / (M h) (``FD/dmap.py:221-261``).
+    mode "doob": DMAP with h: M_h v = M (h v) / (M h) (``FD/dmap.py:221-261``);
+    mode "doob_sym": S M S with S = sqrt(h / (M h)), symmetric and similar to M_h
+                 (same eigenvalues; eigenvectors y = x / sqrt(h M h)), the form a
+                 symmetric Lanczos solves.
     Every rank holds all of K and owns a contiguous block of 256-row tiles of Q.
     """
 
@@ -130,9 +133,9 @@ class ShardedOperator:
                  precision: str = "f16", mode: str = "dmap", h: Optional[torch.Tensor] = None, group=None):
         from . import native
         from .kernel import GaussianOperator
-        if mode not in ("dmap", "amap", "doob"):
-            raise ValueError(f"mode must be dmap, amap or doob (got {mode!r})")
-        if mode == "doob" and h is None:
+        if mode not in ("dmap", "amap", "doob", "doob_sym"):
+            raise ValueError(f"mode must be dmap, amap, doob or doob_sym (got {mode!r})")
+        if mode in ("doob", "doob_sym") and h is None:
             raise ValueError("mode 'doob' needs h")
         self.mode = mode
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -172,9 +175,15 @@ class ShardedOperator:
             _, rs = native.dmap_rscale(Kw, w)
             a, b = self.rows
             self.rscale_k, self.rscale_q = rs, rs[a:b].contiguous()
-            if self.mode == "doob":
+            if self.mode in ("doob", "doob_sym"):
                 self.ph = self.op.apply(self.h, col_scale=rs, row_scale=self.rscale_q,
                                         out_dtype=torch.float32)[:, 0].contiguous()
+            if self.mode == "doob_sym":
+                ph = self.gather(self.ph).contiguous()
+                s_full = (rs.double() * torch.sqrt(self.h.double() / ph.double())).float().contiguous()
+                self.rscale_k, self.rscale_q = s_full, s_full[a:b].contiguous()
+                self.h = None
+                self.ph = None
         return self
 
     def matvec_local(self, v: torch.Tensor, out_dtype=torch.float64) -> torch.Tensor:

@@ -236,13 +236,18 @@ def lobpcg_eigsh(matvec, N: int, k: int = 8, tol: float = 1e-8, maxiter: int = 3
     return (*out, info) if return_info else out
 
 
-def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: int, device, info: SolveInfo):
+def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: int, device, info: SolveInfo,
+                guard: int = 0):
     """LOBPCG iteration (largest eigenvalues) with Rayleigh-Ritz on span[X, R, P].
 
     X0 = QR(N(0,1) block) seeded like the reference.  The trial basis is
     orthonormalised by QR (twice); A is applied to the R and P parts only,
-    A X being carried over.  Returns (vals desc host, vecs device).
+    A X being carried over.  ``guard`` extra columns ride along (faster
+    convergence of clustered spectra); convergence is judged on the top k.
+    Returns (vals desc host (k,), vecs device (N, k)).
     """
+    kk = k
+    k = k + guard
     rng = np.random.default_rng(seed)
     X = torch.from_numpy(np.linalg.qr(rng.standard_normal((N, k)))[0]).to(device)
     AX = block_matvec(X).to(torch.float64)
@@ -253,7 +258,9 @@ def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: in
         G = 0.5 * (G + G.T)
         R = AX - X @ G
         rn = torch.linalg.vector_norm(R, dim=0)
-        info.residuals = (rn / torch.diagonal(G).abs().clamp_min(1e-300)).cpu().numpy()
+        lam = torch.diagonal(G)
+        top = torch.argsort(lam, descending=True)[:kk]
+        info.residuals = (rn[top] / lam[top].abs().clamp_min(1e-300)).cpu().numpy()
         if float(info.residuals.max()) <= tol:
             info.converged = True
             break
@@ -273,5 +280,5 @@ def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: in
         info.n_restart = it + 1
     G = X.T @ AX
     w, Z = torch.linalg.eigh(0.5 * (G + G.T))
-    order = torch.argsort(w, descending=True)
+    order = torch.argsort(w, descending=True)[:kk]
     return w[order].cpu().numpy(), X @ Z[:, order]

@@ -283,3 +283,40 @@ def test_f16x3_tensor_core_fp32_class_at_c2_shape():
     out = op.apply(torch.from_numpy(v).cuda(), out_dtype=torch.float64)[:, 0].cpu().numpy()
     rows = np.random.default_rng(6).choice(X.shape[0], 200, replace=False)
     assert rel_l2(out[rows], exact_apply(X[rows], X, v[:, None], beta)[:, 0]) <= 1e-5
+
+
+@pytest.mark.parametrize("prec", ["f16x3", "f16"])
+def test_lobpcg_block_operator_vs_dense(prec):
+    """LOBPCG on the block (r = k) tensor-core path against dense eigenvalues of the oracle operator."""
+    from flashdiffusion_b200 import GaussianOperator, lobpcg_eigsh
+    from flashdiffusion_b200.kernel_cuda_sm100 import CUDAStateSM100, normalise
+    from tests.golden.make_golden import test_roll
+    X = test_roll(2500, seed=3)
+    op = GaussianOperator(X, None, 1.0, prec)
+    D, Da, rs = normalise(op, 0.5)
+    st = CUDAStateSM100(op, rs, D, Da, 1.0, 0.5)
+    vals, _, info = lobpcg_eigsh(st, X.shape[0], k=8, tol=1e-6 if prec == "f16x3" else 1e-3, maxiter=500,
+                                 return_info=True)
+    M, _ = O.dense_dmap_operator(X, 1.0, 0.5)
+    ref = np.sort(np.linalg.eigvalsh(M))[::-1][:8]
+    assert abs(vals[0] - 1.0) < (3e-6 if prec == "f16x3" else 1e-3)
+    np.testing.assert_allclose(vals, ref, rtol=1e-5 if prec == "f16x3" else 2e-3)
+
+
+@pytest.mark.parametrize("prec", ["f16", "f16x3"])
+def test_block_path_no_drift_over_many_key_tiles(prec):
+    """M sqrt(D_alpha) = sqrt(D_alpha) exactly; the block (r > 1) path must keep that over 2,048 key tiles.
+
+    A single tensor-core accumulator summed over every key tile drifted low (relative 1.7e-3 at
+    262,144 keys); the r = 1 path holds 4e-8 on the same input.  Both columns are checked.
+    """
+    from flashdiffusion_b200 import GaussianOperator, synthetic
+    from flashdiffusion_b200.kernel_cuda_sm100 import normalise
+    X, beta = synthetic.tanh_manifold(n=262_144, d=128 if prec == "f16" else 64, seed=0)
+    op = GaussianOperator(X, None, beta, prec)
+    _, Da, rs = normalise(op, 0.5)
+    x = torch.sqrt(Da.double())
+    Y = op.apply(torch.stack([x, -3.0 * x], 1), col_scale=rs, row_scale=rs, out_dtype=torch.float64)
+    for c, s in enumerate((1.0, -3.0)):
+        err = float(torch.linalg.vector_norm(Y[:, c] - s * x) / torch.linalg.vector_norm(s * x))
+        assert err <= 2e-5, (c, err)
