@@ -40,6 +40,9 @@ CONFIGS = {
                n=500_000, d=66, r=1, mode="doob"),
     "c5": dict(workload="c5: DMAP block matvec, tanh manifold N=1000000 d=128, r=32, alpha=0.5",
                n=1_000_000, d=128, r=32, mode="dmap"),
+    # the north-star target: the single-vector DMAP matvec at the configuration-5 size
+    "c5r1": dict(workload="c5r1: DMAP matvec, tanh manifold N=1000000 d=128, r=1, alpha=0.5",
+                 n=1_000_000, d=128, r=1, mode="dmap"),
 }
 
 

@@ -67,7 +67,7 @@ constexpr uint32_t BOX_BYTES = 128 * 128;  // query box: 128 rows x 64 16-bit co
 constexpr uint32_t KBOX_BYTES = BN * 128;  // key box: BN rows x 64 16-bit columns
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSB = NEPI_WG;               // TMEM S/P buffers of BN columns, one per epilogue warpgroup
-constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 3 RP)
+constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 4 RP)
 constexpr int NEPI_WARPS = 4 * NEPI_WG;
 // O is restarted every `ogroup` key tiles and the group sums are added on the
 // CUDA cores in fp32 (round to nearest): the tensor-core accumulation rounds
@@ -98,7 +98,7 @@ struct Cfg {
     static constexpr uint32_t SMEM_BYTES = MISC_OFF + 16;
     static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
     static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
-    static_assert(O_COL + 3 * RP <= TMEM_COLS, "TMEM budget");
+    static_assert(O_COL + 4 * RP <= TMEM_COLS, "TMEM budget");
 };
 
 // Load `RP / 4` consecutive O columns of this thread's row.
@@ -156,13 +156,23 @@ __device__ __forceinline__ void exp2_to_f16x2(const uint32_t (&v)[16], uint32_t 
     }
 }
 
+// 16 S values -> P = 2^S rounded once to fp16, 8 registers, key 2c in the low half.
+__device__ __forceinline__ void exp2_to_f16(const uint32_t (&v)[16], uint32_t (&p)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const __half2 h = __floats2half2_rn(ptx::ex2_mufu(__uint_as_float(v[2 * i])),
+                                            ptx::ex2_mufu(__uint_as_float(v[2 * i + 1])));
+        p[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+}
+
 template <int KF, int NW, int RP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                 const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
                 const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
                 int64_t nq, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
-                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2, int ogroup) {
+                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2, int ogroup, int three) {
     using C = Cfg<KF, NW, RP>;
     using G = typename C::G;
     extern __shared__ uint8_t smem_raw[];
@@ -301,15 +311,19 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             FD_WAIT(11, &done[q], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else if (warp == PV_WARP0 || warp == PV_WARP1) {
-        // ---- P.U issuers: warp PV_WARP0 runs O1 += P_hi [U_hi; U_lo] (N = 2 RP),
-        //      warp PV_WARP1 runs O2 += P_lo U_hi (N = RP); each tcgen05.mma costs
-        //      its issuing thread ~100 cycles, so independent chains get their
-        //      own issuing warps
+        // ---- P.U issuers.  Three products (fp32-class tiles): warp PV_WARP0 runs
+        //      O1 += P_hi [U_hi; U_lo] (N = 2 RP), warp PV_WARP1 O2 += P_lo U_hi
+        //      (N = RP).  Two products (16-bit tiles, P rounded once to fp16):
+        //      both run P [U_hi; U_lo], warp PV_WARP0 over keys 0-63 of the tile
+        //      into O1, warp PV_WARP1 over keys 64-127 into O2.  Each
+        //      tcgen05.mma costs its issuing thread ~100 cycles, so independent
+        //      chains get their own issuing warps.
         if (lane == 0) {
             const int t = warp - PV_WARP0;
             const uint32_t u_base = ptx::smem_u32(base + C::U_OFF);
-            const uint32_t idesc = t == 0 ? idesc_pv2 : idesc_pv;
+            const uint32_t idesc = (t == 0 || !three) ? idesc_pv2 : idesc_pv;
             const uint32_t dcol = tmem + O_COL + (t == 0 ? 0u : 2u * RP);
+            const int ks0 = three ? 0 : t * (BN / 32), ks1 = three ? BN / 16 : ks0 + BN / 32;
             int ustage = 0;
             uint32_t uph = 0, ocount = 0;
             bool fresh = true;
@@ -323,12 +337,12 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 if (fresh && !FD_WAIT(5, oempty, (ocount & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::tc_fence_after();
                 const uint32_t ut = u_base + ustage * C::USTAGE_BYTES;
-                for (int ks = 0; ks < BN / 16; ++ks) {
+                for (int ks = ks0; ks < ks1; ++ks) {
                     // U_hi^T rows then U_lo^T rows of this 64-key box: one 2 RP-row operand
                     const uint32_t off = (ks >> 2) * 2 * C::UT_BOX + (ks & 3) * 32;
-                    // keys 16ks..16ks+15: P_hi in 8 columns, P_lo in the next 8
-                    const uint32_t a = tmem + pb * BN + ks * 16 + (t == 0 ? 0u : 8u);
-                    ptx::umma_ts(dcol, a, ptx::sw128_kmajor_desc(ut + off), idesc, (fresh && ks == 0) ? 0u : 1u);
+                    // keys 16ks..16ks+15: P (or P_hi) in 8 columns, P_lo in the next 8
+                    const uint32_t a = tmem + pb * BN + ks * 16 + ((t == 0 || !three) ? 0u : 8u);
+                    ptx::umma_ts(dcol, a, ptx::sw128_kmajor_desc(ut + off), idesc, (fresh && ks == ks0) ? 0u : 1u);
                 }
                 fresh = false;
                 ptx::umma_commit(&sempty[pb]);
@@ -373,18 +387,32 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 uint32_t va[16], vb[16], ph[8], pl[8];
                 ptx::tmem_ld16(tb, va);
                 ptx::tmem_wait_ld16(va);
+                if (three) {
 #pragma unroll 1
-                for (int c = 0; c < BN / 16; c += 2) {
-                    ptx::tmem_ld16(tb + (c + 1) * 16, vb);
-                    exp2_to_f16x2(va, ph, pl);
-                    tmem_st8(tb + c * 16, ph);
-                    tmem_st8(tb + c * 16 + 8, pl);
-                    ptx::tmem_wait_ld16(vb);
-                    if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
-                    exp2_to_f16x2(vb, ph, pl);
-                    tmem_st8(tb + (c + 1) * 16, ph);
-                    tmem_st8(tb + (c + 1) * 16 + 8, pl);
-                    if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
+                    for (int c = 0; c < BN / 16; c += 2) {
+                        ptx::tmem_ld16(tb + (c + 1) * 16, vb);
+                        exp2_to_f16x2(va, ph, pl);
+                        tmem_st8(tb + c * 16, ph);
+                        tmem_st8(tb + c * 16 + 8, pl);
+                        ptx::tmem_wait_ld16(vb);
+                        if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                        exp2_to_f16x2(vb, ph, pl);
+                        tmem_st8(tb + (c + 1) * 16, ph);
+                        tmem_st8(tb + (c + 1) * 16 + 8, pl);
+                        if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
+                    }
+                } else {
+#pragma unroll 1
+                    for (int c = 0; c < BN / 16; c += 2) {
+                        ptx::tmem_ld16(tb + (c + 1) * 16, vb);
+                        exp2_to_f16(va, ph);
+                        tmem_st8(tb + c * 16, ph);
+                        ptx::tmem_wait_ld16(vb);
+                        if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                        exp2_to_f16(vb, ph);
+                        tmem_st8(tb + (c + 1) * 16, ph);
+                        if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
+                    }
                 }
                 ptx::tmem_wait_st();
                 ptx::tc_fence_before();
@@ -400,15 +428,25 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 ++ogroups;
                 ptx::tc_fence_after();
                 const int c0 = wg * NC;
-                float o[NC], o2[NC], o3[NC];
-                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);             // P_hi U_hi
-                tmem_ld_cols<NC>(t_lane + O_COL + RP + c0, o2);       // P_hi U_lo
-                tmem_ld_cols<NC>(t_lane + O_COL + 2 * RP + c0, o3);   // P_lo U_hi
+                // three products: P_hi U_hi, P_hi U_lo, P_lo U_hi; two: P U_hi and
+                // P U_lo over keys 0-63, then over keys 64-127
+                float o[NC], o2[NC];
+                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);
+                tmem_ld_cols<NC>(t_lane + O_COL + 2 * RP + c0, o2);
+#pragma unroll
+                for (int i = 0; i < NC; ++i) o[i] += o2[i];
+                tmem_ld_cols<NC>(t_lane + O_COL + RP + c0, o2);
+                if (!three) {
+                    float o4[NC];
+                    tmem_ld_cols<NC>(t_lane + O_COL + 3 * RP + c0, o4);
+#pragma unroll
+                    for (int i = 0; i < NC; ++i) o2[i] += o4[i];
+                }
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(oempty);
 #pragma unroll
-                for (int i = 0; i < NC; ++i) oacc[i] += o[i] + (o2[i] + o3[i]);
+                for (int i = 0; i < NC; ++i) oacc[i] += o[i] + o2[i];
             }
             if (seg_last && wg < 2) {
                 const int c0 = wg * NC;
@@ -489,6 +527,7 @@ struct BlockArgs {
     RowEpilogue ep;
     double* part;
     int ogroup;
+    int three;
 };
 
 template <int KF, int NW, int RP>
@@ -500,13 +539,13 @@ static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
                                      (int)C::SMEM_ALLOC));
     tcb::tc_block_kernel<KF, NW, RP><<<a.sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(
         a.mq, a.mk, a.mqn, a.mkn, a.mu, a.colscale, a.rc, a.nq, a.iqk, a.ipv, a.sc, a.ep, a.part, status,
-        ptx::idesc_f32acc(tcb::BM, 2 * RP, true), a.ogroup);
+        ptx::idesc_f32acc(tcb::BM, 2 * RP, true), a.ogroup, a.three);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
 
-// Columns of U per launch: the three accumulator blocks (3 x 32) fit next to
-// the three 128-column S buffers in the 512 TMEM columns.
+// Columns of U per launch: the accumulator blocks (4 x 32) fit next to the
+// three 128-column S buffers in the 512 TMEM columns.
 int block_max_cols(int d) { (void)d; return 32; }
 
 // Key tiles per O accumulation group: 8 for the 16-bit tiles (bias 6e-6 against
@@ -518,6 +557,17 @@ static int block_ogroup(int tile) {
         if (g >= 1 && g <= 64) return g;
     }
     return tile == FD_TILE_F16X3 ? 1 : 8;
+}
+
+// Products per P.U: 3 (P_hi U_hi + P_hi U_lo + P_lo U_hi: P and U both to
+// ~22 bits) by default.  FD_BLOCK_PRODUCTS=2 rounds P once to fp16 for the
+// 16-bit tiles (P U_hi + P U_lo, half the P.U instructions): about 2^-12
+// relative noise per kernel value, which a column whose sum cancels heavily
+// can amplify past 2e-3.
+static int block_products(int tile) {
+    if (tile == FD_TILE_F16X3) return 3;
+    if (const char* e = getenv("FD_BLOCK_PRODUCTS")) return atoi(e) == 2 ? 2 : 3;
+    return 3;
 }
 
 template <int KF, int NW>
@@ -563,6 +613,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     a.nq = nq;
     a.ep = ep;
     a.ogroup = block_ogroup(tile);
+    a.three = block_products(tile) == 3;
     switch (kf * 100 + nw) {
         case 16: FD_TRY((launch_block_kb<0, 16>(rp, a, s))); break;
         case 32: FD_TRY((launch_block_kb<0, 32>(rp, a, s))); break;
