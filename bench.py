@@ -2,7 +2,7 @@
 
 Workload (default, ``--config c2``): configuration 2 of the benchmark set —
 N = 200,000 points in d = 64 from a seeded 10-component Gaussian mixture,
-median-rule beta, alpha = 0.5, one N(0,1) right-hand side; bf16 tensor-core
+median-rule beta, alpha = 0.5, one N(0,1) right-hand side; fp16 tensor-core
 tiles, fp32 accumulation.  A step is one normalised DMAP matvec
 out = rscale * K(rscale * v) over all N x N pairs (row-sharded over the GPUs
 for N > 1, followed by the NCCL all-gather of the output shards).
@@ -82,20 +82,73 @@ def make_data(cfg, seed=0):
     return X, None, beta, None
 
 
-def cpu_sample(Q, K, beta, rows, r=1, seed=0):
-    """Time the reference algorithm (NumPy tile loop) on `rows` seeded query rows x all keys.
+def _cpu_attach(spec):
+    from multiprocessing import shared_memory
+    shm = shared_memory.SharedMemory(name=spec[0])
+    return shm, np.ndarray(spec[1], dtype=np.float32, buffer=shm.buf)
 
-    Returns (evals/s, seconds, rows).  The row/column scales are set to ones
-    for the sample: they cost O(N) and do not change the tile loop timed."""
+
+def _cpu_worker(job):
+    """One host process: the reference tile loop on a block of query rows (timed inside)."""
+    from threadpoolctl import threadpool_limits
     from oracle import fd_oracle as O
-    K = Q if K is None else K
-    idx = np.sort(np.random.default_rng(seed).choice(Q.shape[0], rows, replace=False))
+    qspec, kspec, idx, beta, r, seed = job
+    qs, Q = _cpu_attach(qspec)
+    ks, K = (qs, Q) if kspec is None else _cpu_attach(kspec)
     v = np.random.default_rng(seed + 1).standard_normal((K.shape[0], r))
-    O.flash_diffusion(Q[idx[:64]], K[:4096], v[:4096], beta)          # warm BLAS threads
-    t0 = time.perf_counter()
-    O.flash_diffusion(Q[idx], K, v, beta)
-    dt = time.perf_counter() - t0
-    return rows * K.shape[0] / dt, dt, rows
+    with threadpool_limits(limits=1):
+        t0 = time.perf_counter()
+        O.flash_diffusion(Q[idx], K, v, beta)
+        dt = time.perf_counter() - t0
+    del Q, K
+    qs.close()
+    if kspec is not None:
+        ks.close()
+    return dt
+
+
+class CpuSampler:
+    """Times the reference algorithm (NumPy tile loop of ``oracle/fd_oracle.py``) on
+    seeded query rows x all keys, split over one host process per core (NumPy
+    holds the GIL between its calls, so threads do not scale; each process
+    keeps BLAS to one thread).  Q and K sit in shared memory.  The row/column
+    scales are ones: they cost O(N) and do not change the tile loop timed."""
+
+    def __init__(self, Q, K, beta, r=1, procs=None):
+        import multiprocessing as mp
+        from multiprocessing import shared_memory
+        self.beta, self.r, self.nq = beta, r, Q.shape[0]
+        self.nk = Q.shape[0] if K is None else K.shape[0]
+        self.procs = max(1, procs or os.cpu_count() or 1)
+        self.shms, self.specs = [], []
+        for A in (Q, K):
+            if A is None:
+                self.specs.append(None)
+                continue
+            A = np.ascontiguousarray(A, dtype=np.float32)
+            shm = shared_memory.SharedMemory(create=True, size=max(A.nbytes, 1))
+            np.ndarray(A.shape, dtype=np.float32, buffer=shm.buf)[...] = A
+            self.shms.append(shm)
+            self.specs.append((shm.name, A.shape))
+        self.pool = mp.get_context("spawn").Pool(self.procs)
+
+    def sample(self, rows, seed=0):
+        """(evals/s, seconds, processes) for `rows` seeded rows x all keys (wall clock over the pool)."""
+        idx = np.sort(np.random.default_rng(seed).choice(self.nq, rows, replace=False))
+        parts = [p_ for p_ in np.array_split(idx, self.procs) if p_.size]
+        jobs = [(self.specs[0], self.specs[1], p_, self.beta, self.r, seed) for p_ in parts]
+        self.pool.map(_cpu_worker, [(j[0], j[1], j[2][:4], j[3], j[4], j[5]) for j in jobs])   # warm
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_worker, jobs, chunksize=1)
+        dt = time.perf_counter() - t0
+        return rows * self.nk / dt, dt, len(parts)
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+        for shm in self.shms:
+            shm.close()
+            shm.unlink()
 
 
 class ClockSampler:
@@ -168,21 +221,24 @@ def run_reference(args):
         return
     cfg = CONFIGS[args.config]
     Q, K, beta, _ = make_data(args.config)
-    rows = args.cpu_rows or (256 if args.config == "c2" else 64)
-    cores = os.cpu_count()
+    cs = CpuSampler(Q, K, beta, cfg["r"])
+    rows = args.cpu_rows or 64 * cs.procs
     for _ in range(args.warmup):
-        cpu_sample(Q, K, beta, min(rows, 64), cfg["r"])
-    vals = [cpu_sample(Q, K, beta, rows, cfg["r"], seed=s_)[0] for s_ in range(args.steps)]
-    v = float(np.mean(vals))
+        cs.sample(min(rows, 8 * cs.procs))
+    res = [cs.sample(rows, seed=s_) for s_ in range(args.steps)]
+    cs.close()
+    v = float(np.mean([x[0] for x in res]))
+    cores = res[0][2]
     n = cfg["n"]
     line = {"impl": "reference", "metric": "kernel evals/sec per matvec (N^2/t)", "value": v, "unit": "evals/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * n * n / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 GEMM + f64 exp/accumulate", "data": "synthetic (seeded generator)",
             "config": {"workload": cfg["workload"], "n": n, "d": cfg["d"], "r": cfg["r"], "sample_rows": rows,
-                       "parallelism": "host BLAS threads"},
+                       "parallelism": "host processes, one BLAS thread each"},
             "cpu_baseline": {"value": v, "unit": "evals/s", "cores": cores, "kind": "port",
-                             "sample": f"{rows} seeded rows x all {n} keys per step, extrapolated to N^2"},
+                             "sample": f"{rows} seeded rows x all {n} keys per step over {cores} processes, "
+                                       "scaled to evals/s"},
             "e2e": {"value": v, "unit": "evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -334,8 +390,20 @@ def run_ours(args):
     mufu_peak = 16 * 148 * sm_max * 1e6          # ex2 per s at max SM clock (measured 15.9/clk/SM)
     tensor_peak_evals = bf16_tf * 1e12 / flops_per_eval
     peak_evals = min(mufu_peak, tensor_peak_evals)
-    cpu_rows = args.cpu_rows or (256 if nk <= 200_000 else 64)
-    cpu_ev, cpu_dt, _ = cpu_sample(Q, K, beta, cpu_rows, r)
+    cpu_baseline = None
+    if world == 1:   # the host baseline is taken on rank 0 of a 1-GPU run only
+        cs = CpuSampler(Q, K, beta, r)
+        if args.cpu_rows:
+            cpu_rows = args.cpu_rows
+        else:   # calibrate, then size the sample to about 10 s of CPU work
+            cal = max(64, 8 * cs.procs)
+            _, dtc, _ = cs.sample(cal)
+            cpu_rows = int(min(nq, max(cal, cal * 10.0 / max(dtc, 1e-3))) // 64 * 64)
+        cpu_ev, cpu_dt, cpu_procs = cs.sample(cpu_rows)
+        cs.close()
+        cpu_baseline = {"value": cpu_ev, "unit": "evals/s", "cores": cpu_procs, "kind": "port",
+                        "sample": f"{cpu_rows} seeded rows x all {nk} keys, r={r}: NumPy tile loop of the reference "
+                                  f"algorithm, {cpu_procs} processes, {cpu_dt:.1f} s, scaled to evals/s"}
     line = {
         "metric": "kernel evals/sec per matvec (N^2/t)", "value": value, "unit": "evals/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
@@ -354,8 +422,7 @@ def run_ours(args):
                      "tensor": {"achieved": kern_evals * flops_per_eval / 1e12, "peak": bf16_tf, "unit": "TFLOP/s",
                                 "frac": kern_evals * flops_per_eval / 1e12 / bf16_tf, "peak_source": peak_src},
                      "frac_at_sampled_clock": kern_evals / min(16 * 148 * sm_clock * 1e6, tensor_peak_evals)},
-        "cpu_baseline": {"value": cpu_ev, "unit": "evals/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{cpu_rows} seeded rows x all {nk} keys, r={r} (NumPy tile loop of the reference algorithm), {cpu_dt:.1f}s"},
+        "cpu_baseline": cpu_baseline,
         "e2e": {"value": evals / e2e_s, "unit": "evals/s", "h2d_bytes_per_step": 8 * nk * r,
                 "d2h_bytes_per_step": 8 * nq * r},
         "gpu_launches": (3 if r == 1 else 4) * args.steps,
