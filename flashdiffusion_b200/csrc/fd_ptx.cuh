@@ -63,6 +63,31 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* b, uint32_t parity, volat
     }
 }
 
+// Shared-memory sequence flags (release / acquire at CTA scope).
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+// Wait until *p >= target, bounded like wait_bounded.
+__device__ __forceinline__ bool wait_seq(const uint32_t* p, uint32_t target, volatile int* abort, int* status,
+                                         uint64_t limit_ns) {
+    if (ld_acquire_u32(p) >= target) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (ld_acquire_u32(p) >= target) return true;
+        if (*abort) return false;
+        if (globaltimer() - t0 > limit_ns) {
+            *abort = 1;
+            atomicExch(status, 4 /* FD_ERR_TIMEOUT */);
+            return false;
+        }
+    }
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
     asm volatile(

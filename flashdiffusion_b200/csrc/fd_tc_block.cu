@@ -49,8 +49,13 @@ __device__ __forceinline__ bool timed_wait(int slot, uint64_t* b, uint32_t ph, v
     return ok;
 }
 #define FD_WAIT(slot, ...) timed_wait(slot, __VA_ARGS__)
+#define FD_SPAN_BEGIN const long long span_t0 = clock64()
+#define FD_SPAN_END(slot) \
+    if (blockIdx.x == 0) atomicAdd(&g_wait_cycles[slot], (unsigned long long)(clock64() - span_t0))
 #else
 #define FD_WAIT(slot, ...) ptx::wait_bounded(__VA_ARGS__)
+#define FD_SPAN_BEGIN
+#define FD_SPAN_END(slot)
 #endif
 
 using tc::Sched;
@@ -62,13 +67,13 @@ constexpr int TMA_WARP = 12;
 constexpr int MMA_WARP = 13;               // Q.K^T issuer of even tiles (and TMEM owner); 14: odd tiles
 constexpr int PV_WARP0 = 15;               // P_hi . [U_hi; U_lo] issuer
 constexpr int PV_WARP1 = 16;               // P_lo . U_hi issuer
-constexpr int NTHREADS = 17 * 32;
+constexpr int UTMA_WARP = 17;              // U^T tile loads (own thread, so a full U ring never delays K)
+constexpr int NTHREADS = 18 * 32;
 constexpr uint32_t BOX_BYTES = 128 * 128;  // query box: 128 rows x 64 16-bit columns
 constexpr uint32_t KBOX_BYTES = BN * 128;  // key box: BN rows x 64 16-bit columns
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int NSB = NEPI_WG;               // TMEM S/P buffers of BN columns, one per epilogue warpgroup
 constexpr uint32_t O_COL = NSB * BN;       // accumulators O1 [384, 384 + 2 RP) and O2 [384 + 2 RP, 384 + 4 RP)
-constexpr int NEPI_WARPS = 4 * NEPI_WG;
 // O is restarted every `ogroup` key tiles and the group sums are added on the
 // CUDA cores in fp32 (round to nearest): the tensor-core accumulation rounds
 // toward zero, so one TMEM accumulator summed over thousands of P.U products
@@ -87,14 +92,21 @@ struct Cfg {
     static constexpr uint32_t STAGE_BYTES = G::bytes(BN);
     static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX;
     static constexpr uint32_t BUDGET = 222u * 1024u - Q_BYTES;
-    static constexpr int USTAGES = 4;              // U^T tiles live from their load to their P.U
-    static constexpr int K_RAW = (int)((BUDGET - USTAGES * USTAGE_BYTES) / STAGE_BYTES);
+    static constexpr uint32_t ACC_BYTES = RP * BM * 4;     // running O sums of the segment
+    // U^T tiles live from their load to their P.U: 4 stages unless that leaves
+    // fewer than 3 K stages
+    static constexpr int USTAGES =
+        (BUDGET - ACC_BYTES - 4 * USTAGE_BYTES) / STAGE_BYTES >= 3 ? 4 : 3;
+    static constexpr int K_RAW = (int)((BUDGET - ACC_BYTES - USTAGES * USTAGE_BYTES) / STAGE_BYTES);
     static constexpr int STAGES = K_RAW > 6 ? 6 : (K_RAW < 2 ? 2 : K_RAW);
     static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
-    static constexpr uint32_t BAR_OFF = U_OFF + USTAGES * USTAGE_BYTES;
-    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[3], sempty[3], pfull[3], ofull, oempty, done[4]
-    static constexpr int NBARS = 2 * STAGES + 2 * USTAGES + 2 + 3 * NSB + 6;
-    static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
+    static constexpr uint32_t ACC_OFF = U_OFF + USTAGES * USTAGE_BYTES;
+    static constexpr uint32_t BAR_OFF = ACC_OFF + ACC_BYTES;
+    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[3], sempty[3], pfull[3], ofull[3],
+    // oempty, done[4]
+    static constexpr int NBARS = 2 * STAGES + 2 * USTAGES + 2 + 4 * NSB + 5;
+    static constexpr uint32_t SEQ_OFF = BAR_OFF + NBARS * 8;
+    static constexpr uint32_t MISC_OFF = SEQ_OFF + BM * 4;
     static constexpr uint32_t SMEM_BYTES = MISC_OFF + 16;
     static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
     static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
@@ -189,9 +201,10 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     uint64_t* sfull = qfull + 2;
     uint64_t* sempty = sfull + NSB;
     uint64_t* pfull = sempty + NSB;
-    uint64_t* ofull = pfull + NSB;
-    uint64_t* oempty = ofull + 1;
+    uint64_t* ofull = pfull + NSB;          // one per epilogue warpgroup: the group's reader
+    uint64_t* oempty = ofull + NSB;
     uint64_t* done = oempty + 1;
+    uint32_t* aseq = (uint32_t*)(base + C::SEQ_OFF);   // per row: O groups added into sacc
     uint32_t* tmem_slot = (uint32_t*)(base + C::MISC_OFF);
     volatile int* abort = (volatile int*)(base + C::MISC_OFF + 4);
 
@@ -220,10 +233,11 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             ptx::mbar_init(&sempty[i], 2);   // both P.U issuers
             ptx::mbar_init(&pfull[i], 4);   // the 4 warps of the warpgroup owning buffer i
         }
-        ptx::mbar_init(ofull, 2);           // both P.U issuers
-        ptx::mbar_init(oempty, 8);          // the two warpgroups that read O
+        for (int i = 0; i < NSB; ++i) ptx::mbar_init(&ofull[i], 2);   // both P.U issuers
+        ptx::mbar_init(oempty, 4);          // the 4 warps of the warpgroup that read O
         for (int i = 0; i < 4; ++i) ptx::mbar_init(&done[i], 1);   // one per MMA issuer
         *abort = 0;
+        for (int i = 0; i < BM; ++i) aseq[i] = 0;
         ptx::fence_mbar_init();
     }
     if (warp == MMA_WARP) {
@@ -233,8 +247,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     if (warp == TMA_WARP && lane == 0) {
         ptx::prefetch_tmap(&tmq);
         ptx::prefetch_tmap(&tmk);
-        ptx::prefetch_tmap(&tmu);
     }
+    if (warp == UTMA_WARP && lane == 0) ptx::prefetch_tmap(&tmu);
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -242,11 +256,10 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
 
     if (warp == TMA_WARP) {
         if (lane == 0) {
-            int stage = 0, ustage = 0;
-            uint32_t kph = 0, uph = 0, qcount = 0;
+            int stage = 0;
+            uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
             int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            uint8_t* sU = base + C::U_OFF;
             for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
                 if (rt != cur_rt) {
                     if (qcount > 0 && !FD_WAIT(0, qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
@@ -264,6 +277,14 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     ptx::tma_load_2d(st + kb * KBOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
                 if (NW) ptx::tma_load_2d(st + KF * KBOX_BYTES, &tmk_n, &kfull[stage], KF * 64, (int)(jt * BN));
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+            }
+        }
+    } else if (warp == UTMA_WARP) {
+        if (lane == 0) {
+            int ustage = 0;
+            uint32_t uph = 0;
+            uint8_t* sU = base + C::U_OFF;
+            for (int64_t n = n0, jt = n0 % n_jt; n < n1; ++n, (++jt == n_jt ? (jt = 0) : 0)) {
                 // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
                 if (!FD_WAIT(2, &uempty[ustage], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 uint8_t* su = sU + ustage * C::USTAGE_BYTES;
@@ -297,11 +318,13 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
                     ptx::tc_fence_after();
                     const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                    FD_SPAN_BEGIN;
 #pragma unroll
                     for (int ks = 0; ks < G::KSTEPS; ++ks)
                         ptx::umma_ss(tmem + b * BN, G::desc(q_base, BM, ks), G::desc(ka, BN, ks), idesc_qk, ks > 0);
                     ptx::umma_commit(&sfull[b]);
                     ptx::umma_commit(&kempty[stage]);
+                    FD_SPAN_END(14);
                 }
                 // both issuers arrive at every row-tile end (qempty counts 2)
                 if ((n + 1 == n1) || (jt + 1 == n_jt)) ptx::umma_commit(qempty);
@@ -337,6 +360,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 if (fresh && !FD_WAIT(5, oempty, (ocount & 1) ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::tc_fence_after();
                 const uint32_t ut = u_base + ustage * C::USTAGE_BYTES;
+                FD_SPAN_BEGIN;
                 for (int ks = ks0; ks < ks1; ++ks) {
                     // U_hi^T rows then U_lo^T rows of this 64-key box: one 2 RP-row operand
                     const uint32_t off = (ks >> 2) * 2 * C::UT_BOX + (ks & 3) * 32;
@@ -347,10 +371,11 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 fresh = false;
                 ptx::umma_commit(&sempty[pb]);
                 ptx::umma_commit(&uempty[ustage]);
+                FD_SPAN_END(13);
                 if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
                 const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
                 if (seg_last || ++gcnt == ogroup) {     // end of an O group
-                    ptx::umma_commit(ofull);
+                    ptx::umma_commit(&ofull[pb]);       // the group's reader: tile m's warpgroup
                     fresh = true;
                     ++ocount;
                     gcnt = 0;
@@ -361,22 +386,28 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         }
     } else {
         // ---- epilogue warpgroups ------------------------------------------
-        const int wg = warp >> 2;             // tiles m = wg (mod 3); O column half wg (wg < 2)
+        // Warpgroup wg turns the S tiles m = wg (mod 3) into P.  At the end of an
+        // O group the warpgroup that made the group's last P reads O (every
+        // column) and adds it into the shared running sum of the segment
+        // (sacc, [RP][BM] fp32); aseq[row] counts the groups added, so the next
+        // group's reader (the thread of the same row in another warpgroup)
+        // waits for it.  Each warpgroup waits on its own ofull barrier, once per
+        // group it reads, so no barrier phase can be skipped.
+        const int wg = warp >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
         const int64_t first_rt = n0 / n_jt;
-        uint32_t ogroups = 0;
+        float* sacc = (float*)(base + C::ACC_OFF);
+        uint32_t ogroups = 0, oread = 0;
         int gcnt = 0;
-        constexpr int NC = RP / 2;
-        float oacc[NC];
-#pragma unroll
-        for (int i = 0; i < NC; ++i) oacc[i] = 0.f;
+        bool seg_fresh = true;
         bool alive = true;
         int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
         for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
             const int64_t m = n - n0;
-            if ((int)(m % NSB) == wg) {
+            const bool mine = (int)(m % NSB) == wg;
+            if (mine) {
                 const int b = wg;
                 if (!FD_WAIT(9, &sfull[b], (uint32_t)((m / NSB) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
@@ -421,52 +452,54 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             }
             const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
             const bool grp_end = seg_last || (++gcnt == ogroup);
-            if (grp_end) gcnt = 0;
-            if (grp_end && wg < 2) {
-                // add this warpgroup's half of the O columns of the finished group
-                if (!FD_WAIT(10, ofull, ogroups & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
-                ++ogroups;
+            if (!grp_end) continue;
+            gcnt = 0;
+            if (mine) {
+                if (!FD_WAIT(10, &ofull[wg], oread & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ++oread;
+                if (!ptx::wait_seq(&aseq[row], ogroups, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
                 ptx::tc_fence_after();
-                const int c0 = wg * NC;
-                // three products: P_hi U_hi, P_hi U_lo, P_lo U_hi; two: P U_hi and
-                // P U_lo over keys 0-63, then over keys 64-127
-                float o[NC], o2[NC];
-                tmem_ld_cols<NC>(t_lane + O_COL + c0, o);
-                tmem_ld_cols<NC>(t_lane + O_COL + 2 * RP + c0, o2);
 #pragma unroll
-                for (int i = 0; i < NC; ++i) o[i] += o2[i];
-                tmem_ld_cols<NC>(t_lane + O_COL + RP + c0, o2);
-                if (!three) {
-                    float o4[NC];
-                    tmem_ld_cols<NC>(t_lane + O_COL + 3 * RP + c0, o4);
+                for (int c16 = 0; c16 < RP; c16 += 16) {
+                    // three products: P_hi U_hi, P_hi U_lo, P_lo U_hi; two: P U_hi and
+                    // P U_lo over keys 0-63, then over keys 64-127
+                    float o[16], t[16];
+                    tmem_ld_cols<16>(t_lane + O_COL + c16, o);
+                    tmem_ld_cols<16>(t_lane + O_COL + 2 * RP + c16, t);
 #pragma unroll
-                    for (int i = 0; i < NC; ++i) o2[i] += o4[i];
+                    for (int i = 0; i < 16; ++i) o[i] += t[i];
+                    tmem_ld_cols<16>(t_lane + O_COL + RP + c16, t);
+                    if (!three) {
+                        float t4[16];
+                        tmem_ld_cols<16>(t_lane + O_COL + 3 * RP + c16, t4);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) t[i] += t4[i];
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float* a = &sacc[(c16 + i) * BM + row];
+                        *a = seg_fresh ? o[i] + t[i] : *a + (o[i] + t[i]);
+                    }
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(oempty);
-#pragma unroll
-                for (int i = 0; i < NC; ++i) oacc[i] += o[i] + o2[i];
-            }
-            if (seg_last && wg < 2) {
-                const int c0 = wg * NC;
-                float o[NC];
-#pragma unroll
-                for (int i = 0; i < NC; ++i) { o[i] = oacc[i]; oacc[i] = 0.f; }
-                const int64_t gi = rt * BM + row;
-                const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
-                const bool full = seg_first == 0 && jt == n_jt - 1;
-                if (gi < nq) {
-#pragma unroll
-                    for (int i = 0; i < NC; ++i) {
-                        const int c = c0 + i;
-                        if (c >= rc) break;
-                        const double val = (double)o[i] * (double)colscale[c];
-                        if (full) store_out(ep, gi, c, val);
-                        else part[(((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * BM + row) * RP + c] = val;
+                if (seg_last) {
+                    const int64_t gi = rt * BM + row;
+                    const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
+                    const bool full = seg_first == 0 && jt == n_jt - 1;
+                    if (gi < nq) {
+                        for (int c = 0; c < rc; ++c) {
+                            const double val = (double)sacc[c * BM + row] * (double)colscale[c];
+                            if (full) store_out(ep, gi, c, val);
+                            else part[(((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * BM + row) * RP + c] = val;
+                        }
                     }
                 }
+                ptx::st_release_u32(&aseq[row], ogroups + 1);
             }
+            ++ogroups;
+            seg_fresh = seg_last;
         }
         ptx::tc_fence_before();
     }
