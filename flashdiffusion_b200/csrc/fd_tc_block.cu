@@ -581,26 +581,24 @@ static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
 // three 128-column S buffers in the 512 TMEM columns.
 int block_max_cols(int d) { (void)d; return 32; }
 
+// Process-wide block-path options (fd_set_block_options); 0 = the default.
+static int g_block_group = 0;
+static int g_block_products = 0;
+
 // Key tiles per O accumulation group: 8 for the 16-bit tiles (bias 6e-6 against
-// their 2e-3 error budget), 1 for the fp32-class tiles (bias 7e-7).
-// FD_BLOCK_OGROUP (1 to 64) overrides it.
+// their 2e-3 error budget), 1 for the fp32-class tiles (bias 8e-7).
 static int block_ogroup(int tile) {
-    if (const char* e = getenv("FD_BLOCK_OGROUP")) {
-        const int g = atoi(e);
-        if (g >= 1 && g <= 64) return g;
-    }
+    if (g_block_group > 0) return g_block_group;
     return tile == FD_TILE_F16X3 ? 1 : 8;
 }
 
 // Products per P.U: 3 (P_hi U_hi + P_hi U_lo + P_lo U_hi: P and U both to
-// ~22 bits) by default.  FD_BLOCK_PRODUCTS=2 rounds P once to fp16 for the
-// 16-bit tiles (P U_hi + P U_lo, half the P.U instructions): about 2^-12
-// relative noise per kernel value, which a column whose sum cancels heavily
-// can amplify past 2e-3.
+// ~22 bits) by default.  2 rounds P once to fp16 for the 16-bit tiles
+// (P U_hi + P U_lo, half the P.U instructions): about 2^-12 relative noise per
+// kernel value, which a column whose sum cancels heavily can amplify past 2e-3.
 static int block_products(int tile) {
     if (tile == FD_TILE_F16X3) return 3;
-    if (const char* e = getenv("FD_BLOCK_PRODUCTS")) return atoi(e) == 2 ? 2 : 3;
-    return 3;
+    return g_block_products == 2 ? 2 : 3;
 }
 
 template <int KF, int NW>
@@ -666,6 +664,16 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
 }
 
 }  // namespace fd
+
+extern "C" int fd_set_block_options(int group_tiles, int products) {
+    if (group_tiles < 0 || group_tiles > 64)
+        return fd::set_error(FD_ERR_ARG, "fd_set_block_options: group_tiles %d (0..64)", group_tiles);
+    if (products != 0 && products != 2 && products != 3)
+        return fd::set_error(FD_ERR_ARG, "fd_set_block_options: products %d (0, 2 or 3)", products);
+    fd::g_block_group = group_tiles;
+    fd::g_block_products = products;
+    return FD_OK;
+}
 
 #ifdef FD_PROFILE_WAITS
 // Read and clear the wait-time counters of the block kernel (profiling builds only).

@@ -237,19 +237,23 @@ def lobpcg_eigsh(matvec, N: int, k: int = 8, tol: float = 1e-8, maxiter: int = 3
 
 
 def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: int, device, info: SolveInfo,
-                guard: int = 0):
+                guard: int = 0, X0: Optional[torch.Tensor] = None):
     """LOBPCG iteration (largest eigenvalues) with Rayleigh-Ritz on span[X, R, P].
 
     X0 = QR(N(0,1) block) seeded like the reference.  The trial basis is
     orthonormalised by QR (twice); A is applied to the R and P parts only,
     A X being carried over.  ``guard`` extra columns ride along (faster
     convergence of clustered spectra); convergence is judged on the top k.
-    Returns (vals desc host (k,), vecs device (N, k)).
+    ``X0`` (N, k + guard) warm-starts the block (e.g. the vectors of a
+    lower-precision stage).  Returns (vals desc host (k,), vecs device (N, k + guard)).
     """
     kk = k
     k = k + guard
-    rng = np.random.default_rng(seed)
-    X = torch.from_numpy(np.linalg.qr(rng.standard_normal((N, k)))[0]).to(device)
+    if X0 is not None:
+        X = torch.linalg.qr(X0.to(device=device, dtype=torch.float64))[0]
+    else:
+        rng = np.random.default_rng(seed)
+        X = torch.from_numpy(np.linalg.qr(rng.standard_normal((N, k)))[0]).to(device)
     AX = block_matvec(X).to(torch.float64)
     info.n_matvec += k
     P = None
@@ -280,5 +284,5 @@ def lobpcg_core(block_matvec, N: int, k: int, tol: float, maxiter: int, seed: in
         info.n_restart = it + 1
     G = X.T @ AX
     w, Z = torch.linalg.eigh(0.5 * (G + G.T))
-    order = torch.argsort(w, descending=True)[:kk]
-    return w[order].cpu().numpy(), X @ Z[:, order]
+    order = torch.argsort(w, descending=True)
+    return w[order[:kk]].cpu().numpy(), X @ Z[:, order]

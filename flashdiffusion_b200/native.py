@@ -45,6 +45,7 @@ SIGNATURES = {
     "fd_apply_noalloc": (_I, [_P, _L, _P, _L, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
     "fd_dmap_weights": (_I, [_P, _L, _F, _P, _P]),
     "fd_dmap_rscale": (_I, [_P, _P, _L, _P, _P, _P]),
+    "fd_set_block_options": (_I, [_I, _I]),
 }
 
 _lib = None
@@ -186,6 +187,11 @@ def dmap_rscale(Kw: torch.Tensor, w: torch.Tensor):
     rs = torch.empty_like(Kw)
     check(load().fd_dmap_rscale(_ptr(Kw), _ptr(w), Kw.numel(), _ptr(Da), _ptr(rs), _stream(Kw.device)))
     return Da, rs
+
+
+def set_block_options(group_tiles: int = 0, products: int = 0) -> None:
+    """Block-path options for later launches (0 = default); see include/fd_sm100.h."""
+    check(load().fd_set_block_options(int(group_tiles), int(products)))
 
 
 def check_status(device=None) -> None:

@@ -171,6 +171,18 @@ int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, int64_t nk, i
                      const float* row_scale, const float* row_div, void* out, int out_dtype,
                      void* stream);
 
+/* Options of the block (r > 1) tensor-core path, process-wide, for the next
+ * launches (no counterpart in the reference, whose GPU path has no block
+ * product).  group_tiles: key tiles summed in one tensor-core accumulator
+ * before the sum moves to fp32 registers (1..64; 0 = default: 8 for the 16-bit
+ * tiles, 1 for FD_TILE_F16X3).  The tensor-core accumulation rounds toward
+ * zero, so fewer tiles per group give a smaller bias (about 7.5e-7 per tile of
+ * group) at some speed.  products: 3 (default, P and U both split hi/lo) or 2
+ * (16-bit tiles only: P rounded once to fp16; faster, 2^-12 noise per kernel
+ * value).  0 restores the default.  Not thread-safe against concurrent
+ * launches from other host threads. */
+int fd_set_block_options(int group_tiles, int products);
+
 /* ---------------------------------------------------------------------------
  * Coifman-Lafon normalisation helpers (FD/dmap.py:108-115,
  * FD/kernel_cuda_sm100.py:89-98), fp32 vectors of length n.
