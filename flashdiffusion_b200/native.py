@@ -46,6 +46,8 @@ SIGNATURES = {
     "fd_dmap_weights": (_I, [_P, _L, _F, _P, _P]),
     "fd_dmap_rscale": (_I, [_P, _P, _L, _P, _P, _P]),
     "fd_set_block_options": (_I, [_I, _I]),
+    "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
+    "fd_pairwise_sqdist": (_I, [_P, _L, _I, _P, _P]),
 }
 
 _lib = None

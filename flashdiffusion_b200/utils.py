@@ -1,0 +1,66 @@
+"""Bandwidth selection and the Nystrom extension (reference ``FD/utils.py``), on the GPU.
+
+``median_bandwidth`` and ``knn_bandwidth`` keep the reference's names, arguments
+and return values; the O(m^2) / O(N^2) distance work runs in libfd_sm100.so
+(``fd_pairwise_sqdist``, ``fd_knn_sqdist``: fp32 coordinate differences on the
+CUDA cores, the k smallest per row kept in registers, so no N x N matrix is
+formed or sorted).  The seeded subsample of the median rule is drawn on the host
+exactly as the reference draws it.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import native
+from .kernel import to_device
+
+__all__ = ["median_bandwidth", "knn_bandwidth", "knn_sqdist", "nystrom_extend"]
+
+
+def median_bandwidth(X, subsample: int = 2000) -> float:
+    """beta = 1 / (2 median(||x_i - x_j||^2 > 0)) over a seeded subsample (``FD/utils.py:16-28``)."""
+    dev = native.require_device()
+    Xh = X.detach().cpu().numpy() if isinstance(X, torch.Tensor) else np.asarray(X)
+    N = Xh.shape[0]
+    if N > subsample:
+        Xh = Xh[np.random.default_rng(0).choice(N, subsample, replace=False)]
+    Xd = to_device(np.ascontiguousarray(Xh), torch.float32, dev).contiguous()
+    m, d = Xd.shape
+    d2 = torch.empty((m, m), dtype=torch.float32, device=dev)
+    native.check(native.load().fd_pairwise_sqdist(native._ptr(Xd), m, d, native._ptr(d2), native._stream(dev)))
+    pos = d2[d2 > 0]
+    if pos.numel() == 0:
+        return 1.0
+    s = torch.sort(pos.double()).values
+    n = s.numel()
+    med = float(s[n // 2]) if n % 2 else 0.5 * float(s[n // 2 - 1] + s[n // 2])
+    return 1.0 / (2.0 * med) if med > 0 else 1.0
+
+
+def knn_sqdist(Q, K=None, k: int = 8) -> torch.Tensor:
+    """(N_q, k) device fp32: the k smallest squared distances of each query row to the keys, ascending."""
+    dev = native.require_device()
+    Qd = to_device(Q, torch.float32, dev).contiguous()
+    Kd = Qd if K is None else to_device(K, torch.float32, dev).contiguous()
+    nq, d = Qd.shape
+    out = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    native.check(native.load().fd_knn_sqdist(native._ptr(Qd), nq, native._ptr(Kd), Kd.shape[0], d, k,
+                                             native._ptr(out), native._stream(dev)))
+    return out
+
+
+def knn_bandwidth(X, k: int = 7) -> np.ndarray:
+    """Self-tuning per-point bandwidth sigma_i = ||x_i - x_(i,k)|| (``FD/utils.py:31-52``).
+
+    Index 0 is the point itself (distance 0), as in the reference's sorted rows.
+    Returns sigma (N,) fp64, floored at 1e-10.
+    """
+    d2 = knn_sqdist(X, None, k + 1)[:, k]
+    return np.maximum(np.sqrt(d2.double().cpu().numpy()), 1e-10)
+
+
+def nystrom_extend(dm, X_new, t: int = 1) -> np.ndarray:
+    """Out-of-sample coordinates of a fitted, transformed DiffusionMap (``FD/utils.py:59-123``)."""
+    return dm.nystrom(X_new, t=t)

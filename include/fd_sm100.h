@@ -171,6 +171,22 @@ int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, int64_t nk, i
                      const float* row_scale, const float* row_div, void* out, int out_dtype,
                      void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Bandwidth selection (FD/utils.py:16-52), fp32 row-major inputs, fp32 CUDA-core
+ * arithmetic on coordinate differences.
+ * ------------------------------------------------------------------------- */
+
+/* out[i][0..k) = the k smallest squared distances from query row i to the key
+ * rows, ascending (a query that is also a key finds itself at 0).  Replaces the
+ * dense sort of knn_bandwidth, FD/utils.py:31-52 (sigma_i = sqrt(out[i][k]) with
+ * k+1 columns).  1 <= k <= 64, k <= nk, 1 <= d <= 1024. */
+int fd_knn_sqdist(const float* Q, int64_t nq, const float* K, int64_t nk, int d, int k, float* out,
+                  void* stream);
+
+/* out[i][j] = ||x_i - x_j||^2 for a sample of m <= 65535 rows (the median
+ * heuristic, median_bandwidth, FD/utils.py:16-28). */
+int fd_pairwise_sqdist(const float* X, int64_t m, int d, float* out, void* stream);
+
 /* Options of the block (r > 1) tensor-core path, process-wide, for the next
  * launches (no counterpart in the reference, whose GPU path has no block
  * product).  group_tiles: key tiles summed in one tensor-core accumulator

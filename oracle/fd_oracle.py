@@ -19,6 +19,8 @@ It restates, in plain NumPy, the reference algorithm of sparsetrace/FlashDiffusi
 * ``dense_kernel`` / ``dense_dmap_operator`` — ``tests/test_kernel.py:17-30``
 * ``lanczos_eigsh``     — ``FD/eigensolver.py:33-85`` (ARPACK IRLM via SciPy, descending sort)
 * ``transform_coords``  — ``FD/dmap.py:184-189``
+* ``median_bandwidth``  — ``FD/utils.py:16-28``   (seeded subsample, median of positive d^2)
+* ``knn_bandwidth``     — ``FD/utils.py:31-52``   (distance to the k-th neighbour, self at index 0)
 
 Parity is pinned: ``tests/test_oracle.py`` checks every function here against
 golden vectors produced by running the reference itself
@@ -33,6 +35,7 @@ __all__ = [
     "dist2_tile", "prepass_rowsum", "flash_diffusion", "dmap_fit", "dmap_matvec",
     "doob_ph", "doob_matvec", "amap_normalise", "nystrom_extend", "dense_kernel",
     "dense_dmap_operator", "lanczos_eigsh", "transform_coords", "sym_doob_operator",
+    "median_bandwidth", "knn_bandwidth", "sq_dists",
 ]
 
 
@@ -188,3 +191,29 @@ def transform_coords(vals, vecs, rscale, t=1):
     psi = vecs / rscale[:, None]
     psi = psi / np.linalg.norm(psi, axis=0, keepdims=True)
     return psi[:, 1:] * (vals[1:] ** t)[None, :]
+
+
+def sq_dists(A, B):
+    """Squared distances by the law of cosines in the inputs' dtype, clamped at 0
+    (the form ``FD/utils.py:23-24,46-47`` use)."""
+    A = np.asarray(A)
+    B = np.asarray(B)
+    return np.maximum((A * A).sum(1)[:, None] + (B * B).sum(1)[None, :] - 2 * A @ B.T, 0)
+
+
+def median_bandwidth(X, subsample=2000):
+    """beta = 1 / (2 median of the positive pairwise d^2) over a seeded subsample
+    (``default_rng(0)``, without replacement, only when N > subsample) — ``FD/utils.py:16-28``."""
+    X = np.asarray(X)
+    if X.shape[0] > subsample:
+        X = X[np.random.default_rng(0).choice(X.shape[0], subsample, replace=False)]
+    d2 = sq_dists(X, X)
+    med = np.median(d2[d2 > 0])
+    return 1.0 / (2.0 * med) if med > 0 else 1.0
+
+
+def knn_bandwidth(X, k=7):
+    """sigma_i = sqrt(k-th smallest d^2 of row i, index 0 being the point itself),
+    floored at 1e-10 — ``FD/utils.py:31-52``."""
+    d2 = np.sort(sq_dists(X, X), axis=1)
+    return np.maximum(np.sqrt(d2[:, k]), 1e-10)

@@ -20,6 +20,7 @@ Fixtures (reference call each one pins):
   nystrom.npz     utils.nystrom_extend (Q != K normalisation), 200 train / 40 new
   gmm64.npz       kernel.FlashDiffusion DMAP matvec at d=64, N=1024 (mixture)
   c1.npz          configuration 1 (Swiss roll N=4096, d=3): fit + Lanczos k=8 eigenvalues
+  bandwidth.npz   utils.median_bandwidth (N=3000 > subsample) and utils.knn_bandwidth (k=7, 5)
 """
 
 from __future__ import annotations
@@ -133,8 +134,22 @@ def main(ref_root):
         dmc.transform()
     np.savez_compressed(os.path.join(HERE, "c1.npz"), X=Xc, beta=bc, D=dmc.D_, rscale=dmc.rscale_,
                         vals=dmc.eigenvalues_)
+    bandwidth(U)
     print("golden fixtures written to", HERE)
 
 
+def bandwidth(U):
+    Xb = np.random.default_rng(21).standard_normal((3000, 5)) * np.array([1.0, 2.0, 0.5, 1.0, 3.0])
+    Xk = Xb[:1200]
+    np.savez_compressed(os.path.join(HERE, "bandwidth.npz"), X=Xb, median_beta=U.median_bandwidth(Xb),
+                        median_beta_small=U.median_bandwidth(Xb[:500]), Xk=Xk,
+                        sigma7=U.knn_bandwidth(Xk, k=7), sigma5=U.knn_bandwidth(Xk, k=5))
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FD_REFERENCE_ROOT", ""))
+    # usage: make_golden.py REFERENCE_ROOT [bandwidth]   (the second form writes bandwidth.npz only)
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FD_REFERENCE_ROOT", "")
+    if len(sys.argv) > 2 and sys.argv[2] == "bandwidth":
+        bandwidth(_ref_modules(root)[3])
+    else:
+        main(root)

@@ -120,3 +120,11 @@ def test_sym_doob_similarity():
     ev = np.sort(np.linalg.eigvals(Mh).real)[::-1]
     es = np.sort(np.linalg.eigvalsh(O.sym_doob_operator(M, h, Ph)))[::-1]
     np.testing.assert_allclose(ev[:6], es[:6], rtol=1e-9)
+
+
+def test_bandwidth_rules_match_reference(gold):
+    g = gold("bandwidth.npz")
+    assert O.median_bandwidth(g["X"]) == pytest.approx(float(g["median_beta"]), rel=RT)
+    assert O.median_bandwidth(g["X"][:500]) == pytest.approx(float(g["median_beta_small"]), rel=RT)
+    np.testing.assert_allclose(O.knn_bandwidth(g["Xk"], k=7), g["sigma7"], rtol=RT)
+    np.testing.assert_allclose(O.knn_bandwidth(g["Xk"], k=5), g["sigma5"], rtol=RT)
