@@ -21,6 +21,7 @@ It restates, in plain NumPy, the reference algorithm of sparsetrace/FlashDiffusi
 * ``transform_coords``  — ``FD/dmap.py:184-189``
 * ``median_bandwidth``  — ``FD/utils.py:16-28``   (seeded subsample, median of positive d^2)
 * ``knn_bandwidth``     — ``FD/utils.py:31-52``   (distance to the k-th neighbour, self at index 0)
+* ``apply_pplus`` / ``carre_du_champ`` / ``metric_tensor`` — ``FD/cdc.py:45-168``
 
 Parity is pinned: ``tests/test_oracle.py`` checks every function here against
 golden vectors produced by running the reference itself
@@ -35,7 +36,7 @@ __all__ = [
     "dist2_tile", "prepass_rowsum", "flash_diffusion", "dmap_fit", "dmap_matvec",
     "doob_ph", "doob_matvec", "amap_normalise", "nystrom_extend", "dense_kernel",
     "dense_dmap_operator", "lanczos_eigsh", "transform_coords", "sym_doob_operator",
-    "median_bandwidth", "knn_bandwidth", "sq_dists",
+    "median_bandwidth", "knn_bandwidth", "sq_dists", "apply_pplus", "carre_du_champ", "metric_tensor",
 ]
 
 
@@ -217,3 +218,30 @@ def knn_bandwidth(X, k=7):
     floored at 1e-10 — ``FD/utils.py:31-52``."""
     d2 = np.sort(sq_dists(X, X), axis=1)
     return np.maximum(np.sqrt(d2[:, k]), 1e-10)
+
+
+def apply_pplus(X, beta, alpha, D, D_alpha, F, tile=512):
+    """P+ F = diag(w / D_alpha) K diag(w) F with w = D^-alpha (``FD/cdc.py:107-130``)."""
+    w = np.asarray(D, np.float64) ** (-alpha)
+    F = np.asarray(F, np.float64)
+    out = flash_diffusion(X, X, F.reshape(F.shape[0], -1), beta, w / np.asarray(D_alpha, np.float64), w, None, tile)
+    return out if F.ndim == 2 else out[:, 0]
+
+
+def carre_du_champ(X, beta, alpha, D, D_alpha, phi_k, phi_l, lambda_k, lambda_l, tile=512):
+    """Gamma(phi_k, phi_l) = (P+(phi_k phi_l) - lambda_k phi_k phi_l - lambda_l phi_l phi_k) / 2,
+    the reference's formula as written (``FD/cdc.py:96-104``)."""
+    pkl = np.asarray(phi_k) * np.asarray(phi_l)
+    return 0.5 * (apply_pplus(X, beta, alpha, D, D_alpha, pkl, tile) - lambda_k * pkl - lambda_l * pkl)
+
+
+def metric_tensor(X, beta, alpha, D, D_alpha, vals, phi, pairs=None, tile=512):
+    """G[i,k,l] = Gamma(phi_k, phi_l)(i) over the pairs (default: all k <= l), symmetric;
+    M = sum_i G_i G_i^T (``FD/cdc.py:133-168``)."""
+    k = len(vals)
+    G = np.zeros((phi.shape[0], k, k))
+    for a, b in (pairs if pairs is not None else [(i, j) for i in range(k) for j in range(i, k)]):
+        g = carre_du_champ(X, beta, alpha, D, D_alpha, phi[:, a], phi[:, b], vals[a], vals[b], tile)
+        G[:, a, b] = g
+        G[:, b, a] = g
+    return G, np.einsum("ikm,ilm->kl", G, G)

@@ -21,6 +21,7 @@ Fixtures (reference call each one pins):
   gmm64.npz       kernel.FlashDiffusion DMAP matvec at d=64, N=1024 (mixture)
   c1.npz          configuration 1 (Swiss roll N=4096, d=3): fit + Lanczos k=8 eigenvalues
   bandwidth.npz   utils.median_bandwidth (N=3000 > subsample) and utils.knn_bandwidth (k=7, 5)
+  cdc.npz         cdc.carre_du_champ and cdc.metric_tensor on a fitted map (N=400, k=5)
 """
 
 from __future__ import annotations
@@ -45,6 +46,24 @@ def _ref_modules(ref_root):
     # The reference dispatcher asks torch for a GPU; force its NumPy path.
     K._get_cuda_backend = lambda: None
     return K, D, E, U
+
+
+def cdc(ref_root):
+    K, D, _, _ = _ref_modules(ref_root)
+    import flashdiffusion.cdc as C             # noqa: E402
+    X = test_roll(400, seed=4)
+    dm = D.DiffusionMap(beta=1.0, alpha=0.5, n_components=5, tile=128)
+    with contextlib.redirect_stdout(io.StringIO()):
+        dm.fit(X)
+        dm.transform()
+    vals = dm.eigenvalues_
+    phi = dm.eigenvectors_ / dm.rscale_[:, None]
+    phi = phi / np.linalg.norm(phi, axis=0, keepdims=True)
+    g13 = C.carre_du_champ(dm, phi[:, 1], phi[:, 3], vals[1], vals[3])
+    G, M = C.metric_tensor(dm, vals, phi)
+    Gp, Mp = C.metric_tensor(dm, vals, phi, pairs=[(1, 1), (1, 2), (0, 4)])
+    np.savez_compressed(os.path.join(HERE, "cdc.npz"), X=X, vals=vals, phi=phi, D=dm.D_, D_alpha=dm.D_alpha_,
+                        gamma13=g13, G=G, M=M, Gp=Gp, Mp=Mp)
 
 
 def test_roll(N, seed=0):
@@ -135,6 +154,7 @@ def main(ref_root):
     np.savez_compressed(os.path.join(HERE, "c1.npz"), X=Xc, beta=bc, D=dmc.D_, rscale=dmc.rscale_,
                         vals=dmc.eigenvalues_)
     bandwidth(U)
+    cdc(ref_root)
     print("golden fixtures written to", HERE)
 
 
@@ -147,9 +167,11 @@ def bandwidth(U):
 
 
 if __name__ == "__main__":
-    # usage: make_golden.py REFERENCE_ROOT [bandwidth]   (the second form writes bandwidth.npz only)
+    # usage: make_golden.py REFERENCE_ROOT [bandwidth|cdc]   (the second form writes that fixture only)
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FD_REFERENCE_ROOT", "")
     if len(sys.argv) > 2 and sys.argv[2] == "bandwidth":
         bandwidth(_ref_modules(root)[3])
+    elif len(sys.argv) > 2 and sys.argv[2] == "cdc":
+        cdc(root)
     else:
         main(root)

@@ -128,3 +128,17 @@ def test_bandwidth_rules_match_reference(gold):
     assert O.median_bandwidth(g["X"][:500]) == pytest.approx(float(g["median_beta_small"]), rel=RT)
     np.testing.assert_allclose(O.knn_bandwidth(g["Xk"], k=7), g["sigma7"], rtol=RT)
     np.testing.assert_allclose(O.knn_bandwidth(g["Xk"], k=5), g["sigma5"], rtol=RT)
+
+
+def test_carre_du_champ_matches_reference(gold):
+    g = gold("cdc.npz")
+    args = (g["X"], 1.0, 0.5, g["D"], g["D_alpha"])
+    vals, phi = g["vals"], g["phi"]
+    np.testing.assert_allclose(O.carre_du_champ(*args, phi[:, 1], phi[:, 3], vals[1], vals[3], tile=128),
+                               g["gamma13"], rtol=1e-9, atol=1e-15)
+    G, M = O.metric_tensor(*args, vals, phi, tile=128)
+    np.testing.assert_allclose(G, g["G"], rtol=1e-9, atol=1e-15)
+    np.testing.assert_allclose(M, g["M"], rtol=1e-9, atol=1e-15)
+    Gp, Mp = O.metric_tensor(*args, vals, phi, pairs=[(1, 1), (1, 2), (0, 4)], tile=128)
+    np.testing.assert_allclose(Gp, g["Gp"], rtol=1e-9, atol=1e-15)
+    np.testing.assert_allclose(Mp, g["Mp"], rtol=1e-9, atol=1e-15)
