@@ -187,6 +187,24 @@ int fd_knn_sqdist(const float* Q, int64_t nq, const float* K, int64_t nk, int d,
  * heuristic, median_bandwidth, FD/utils.py:16-28). */
 int fd_pairwise_sqdist(const float* X, int64_t m, int d, float* out, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * RoPE-DMAP preprocessing (FD/ROPE.py:31-106,231-345).
+ * ------------------------------------------------------------------------- */
+
+/* Y (K x L*D fp32) = K windows of L samples of D features, each centred
+ * ((x - mu[j]) / sigma[j], fp64), with coordinate pairs (2p, 2p+1) rotated by
+ * pos * pos_scale * freqs[p] (fp64 sin/cos).  Window T, sample c, feature j is
+ * read at F[T*sT + c*sC + j] and its position at pos[T*pT + c*pC]: a time series
+ * (N x D) gives its K = N - (L-1) step Hankel windows with sT = D, sC = step*D,
+ * pT = 1, pC = step, without copying them; a (B, L, D) window array has
+ * sT = L*D, sC = D.  window_mode 0 rotates each sample by its own position;
+ * window_mode 1 rotates the flattened window once by the position of sample c_w.
+ * Pairs p >= n_freqs do not rotate; an odd last coordinate is copied.  Replaces
+ * the host make_hankel_windows / _transform_windows chain of FD/ROPE.py. */
+int fd_rope_windows(const double* F, int64_t sT, int64_t sC, const double* pos, int64_t pT, int64_t pC, int64_t K,
+                    int D, int L, int window_mode, int c_w, double pos_scale, const double* freqs, int n_freqs,
+                    const double* mu, const double* sigma, float* Y, void* stream);
+
 /* Options of the block (r > 1) tensor-core path, process-wide, for the next
  * launches (no counterpart in the reference, whose GPU path has no block
  * product).  group_tiles: key tiles summed in one tensor-core accumulator

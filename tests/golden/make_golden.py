@@ -22,6 +22,8 @@ Fixtures (reference call each one pins):
   c1.npz          configuration 1 (Swiss roll N=4096, d=3): fit + Lanczos k=8 eigenvalues
   bandwidth.npz   utils.median_bandwidth (N=3000 > subsample) and utils.knn_bandwidth (k=7, 5)
   cdc.npz         cdc.carre_du_champ and cdc.metric_tensor on a fitted map (N=400, k=5)
+  rope.npz        ROPE encoder: sample mode (D=2, L=6) and window mode (D=3, L=5, step=2, centre),
+                  fitted eigenpairs, psi, beta, encode_series and encode_windows of new data
 """
 
 from __future__ import annotations
@@ -46,6 +48,31 @@ def _ref_modules(ref_root):
     # The reference dispatcher asks torch for a GPU; force its NumPy path.
     K._get_cuda_backend = lambda: None
     return K, D, E, U
+
+
+def rope_series(n, D, seed):
+    rng = np.random.default_rng(seed)
+    t = np.arange(n) * 0.07
+    cols = [np.sin(t * (1 + 0.3 * j)) + 0.05 * rng.standard_normal(n) for j in range(D)]
+    return np.stack(cols, axis=1)
+
+
+def rope(ref_root):
+    sys.path.insert(0, os.path.join(ref_root, "src"))
+    from flashdiffusion.ROPE import ROPE, make_hankel_windows   # noqa: E402
+    F = rope_series(320, 2, 1)
+    Fn = rope_series(120, 2, 2)
+    a = ROPE(F, L=6, rank=4, alpha=1.0, pos_scale=0.5, seed=3)
+    F3 = rope_series(300, 3, 4)
+    Fn3 = rope_series(90, 3, 5)
+    b = ROPE(F3, L=5, rank=3, alpha=0.5, step=2, rope_mode="window", window_position="center", pos_scale=0.2,
+             scale=True, seed=7)
+    Wq = make_hankel_windows(Fn, 6)[:7]
+    Pq = np.arange(7)[:, None] + np.arange(6)[None, :] + 40.0
+    np.savez_compressed(os.path.join(HERE, "rope.npz"), F=F, Fn=Fn, F3=F3, Fn3=Fn3,
+                        a_lam=a.lam_, a_psi=a.psi_, a_beta=a.beta_, a_enc=a.encode_series(Fn),
+                        a_encw=a.encode_windows(Wq, positions=Pq), a_encw0=a.encode_windows(Wq), Wq=Wq, Pq=Pq,
+                        b_lam=b.lam_, b_psi=b.psi_, b_beta=b.beta_, b_enc=b.encode_series(Fn3))
 
 
 def cdc(ref_root):
@@ -155,6 +182,7 @@ def main(ref_root):
                         vals=dmc.eigenvalues_)
     bandwidth(U)
     cdc(ref_root)
+    rope(ref_root)
     print("golden fixtures written to", HERE)
 
 
@@ -167,11 +195,13 @@ def bandwidth(U):
 
 
 if __name__ == "__main__":
-    # usage: make_golden.py REFERENCE_ROOT [bandwidth|cdc]   (the second form writes that fixture only)
+    # usage: make_golden.py REFERENCE_ROOT [bandwidth|cdc|rope]   (the second form writes that fixture only)
     root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FD_REFERENCE_ROOT", "")
     if len(sys.argv) > 2 and sys.argv[2] == "bandwidth":
         bandwidth(_ref_modules(root)[3])
     elif len(sys.argv) > 2 and sys.argv[2] == "cdc":
         cdc(root)
+    elif len(sys.argv) > 2 and sys.argv[2] == "rope":
+        rope(root)
     else:
         main(root)
