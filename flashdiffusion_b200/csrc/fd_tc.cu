@@ -115,8 +115,6 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
-    const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
-    const int64_t n_jt = sc.n_jt;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < C::STAGES; ++i) {
@@ -160,9 +158,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-                const int64_t m = n - n0;
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t m = w.s, rt = w.rt, jt = w.jt;
                 if (rt != cur_rt) {
                     if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
@@ -202,9 +199,8 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-                const int64_t m = n - n0;
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t m = w.s, rt = w.rt;
                 const int p = (int)(m & 1);
                 const uint32_t use = (uint32_t)(m >> 1);
                 if (rt != cur_rt) {
@@ -225,7 +221,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     ptx::umma_commit(&sfull[b]);
                 }
                 ptx::umma_commit(&kempty[stage]);
-                if (n + 1 == n1 || jt + 1 == n_jt) ptx::umma_commit(qempty);
+                if (w.seg_last()) ptx::umma_commit(qempty);
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
             // every MMA issued above has completed once `done` flips
@@ -239,13 +235,11 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
         const int quarter = warp & 3;
         const int row_in_tile = s * BM + quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        const int64_t first_rt = n0 / n_jt;
         double acc = 0.0;
         uint32_t segs = 0;
         bool alive = true;
-        int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
-        for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-            const int64_t m = n - n0;
+        for (Walk w(sc, cta); !w.done() && alive; w.next()) {
+            const int64_t m = w.s, rt = w.rt;
             if ((int)(m & 1) == p) {
                 const uint32_t use = (uint32_t)(m >> 1);
                 const int b = s * 2 + p;
@@ -281,7 +275,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                 ptx::unpack2(acc_b, b0, b1);
                 acc += (double)((__uint_as_float(a0) + __uint_as_float(a1)) + (__uint_as_float(b0) + __uint_as_float(b1)));
             }
-            if (n + 1 == n1 || jt + 1 == n_jt) {
+            if (w.seg_last()) {
                 // combine the two parity halves of this subtile, then store
                 const uint32_t ph = segs & 1;
                 if (p == 1) {
@@ -293,11 +287,9 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     const double tot = acc + red[s * BM + quarter * 32 + lane];
                     ptx::mbar_arrive(&rempty[s]);
                     const int64_t gi = rt * ROWS + row_in_tile;
-                    const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
-                    const bool full = seg_first == 0 && jt == n_jt - 1;
                     if (gi < nq) {
-                        if (full) store_out(ep, gi, 0, tot);
-                        else part[((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * ROWS + row_in_tile] = tot;
+                        if (w.seg_full()) store_out(ep, gi, 0, tot);
+                        else part[((int64_t)cta * 2 + w.slot()) * ROWS + row_in_tile] = tot;
                     }
                 }
                 acc = 0.0;
@@ -316,25 +308,16 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
 // Sum the partials of row tiles cut between CTA ranges, in CTA order.
 __global__ void tc_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, RowEpilogue ep) {
     const int64_t rt = blockIdx.x;
-    const int64_t lo = rt * sc.n_jt, hi = lo + sc.n_jt - 1;
-    auto owner = [&](int64_t n) {
-        int c = (int)(n * sc.grid / sc.units);
-        if (c >= sc.grid) c = sc.grid - 1;
-        while (c + 1 < sc.grid && sc.start(c + 1) <= n) ++c;
-        while (c > 0 && sc.start(c) > n) --c;
-        return c;
-    };
-    const int c_lo = owner(lo), c_hi = owner(hi);
+    int c_lo, c_hi;
+    cut_owners(sc, rt, &c_lo, &c_hi);
     if (c_lo == c_hi) return;
     for (int r = threadIdx.x; r < ROWS; r += blockDim.x) {
         const int64_t gi = rt * ROWS + r;
         if (gi >= nq) continue;
         double sum = 0.0;
         for (int c = c_lo; c <= c_hi; ++c) {
-            const int64_t st = sc.start(c);
-            if (st == sc.start(c + 1)) continue;  // empty range
-            const int slot = (st / sc.n_jt == rt) ? 0 : 1;
-            sum += part[((int64_t)c * 2 + slot) * ROWS + r];
+            if (sc.start(c) == sc.start(c + 1)) continue;  // empty range
+            sum += part[((int64_t)c * 2 + cut_slot(sc, c, rt)) * ROWS + r];
         }
         store_out(ep, gi, 0, sum);
     }
@@ -469,9 +452,7 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
         FD_TRY(make_tile_map(&a.mkn, kop, nk, kd, tc::BN, f16, nw));
     }
     a.idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
-    a.sc.n_jt = cdiv(nk, tc::BN);
-    a.sc.units = cdiv(nq, tc::ROWS) * a.sc.n_jt;
-    a.sc.grid = (int)std::min<int64_t>(num_sms(), a.sc.units);
+    a.sc = tc::Sched::make(cdiv(nq, tc::ROWS), cdiv(nk, tc::BN), num_sms(), (size_t)nk * kd * 2);
     a.part = (double*)ws;
     a.u = (const float*)rhs;
     a.nq = nq;

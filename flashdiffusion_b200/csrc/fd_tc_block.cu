@@ -59,6 +59,9 @@ __device__ __forceinline__ bool timed_wait(int slot, uint64_t* b, uint32_t ph, v
 #endif
 
 using tc::Sched;
+using tc::Walk;
+using tc::cut_owners;
+using tc::cut_slot;
 
 constexpr int BM = 128;
 constexpr int BN = 128;                    // keys per tile (N of Q.K^T, K of P.U)
@@ -211,8 +214,6 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int cta = blockIdx.x;
-    const int64_t n0 = sc.start(cta), n1 = sc.start(cta + 1);
-    const int64_t n_jt = sc.n_jt;
 #ifdef FD_PROFILE_WAITS
     const long long t_start = clock64();
 #endif
@@ -259,8 +260,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t rt = w.rt, jt = w.jt;
                 if (rt != cur_rt) {
                     if (qcount > 0 && !FD_WAIT(0, qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
@@ -284,7 +285,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             int ustage = 0;
             uint32_t uph = 0;
             uint8_t* sU = base + C::U_OFF;
-            for (int64_t n = n0, jt = n0 % n_jt; n < n1; ++n, (++jt == n_jt ? (jt = 0) : 0)) {
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t jt = w.jt;
                 // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
                 if (!FD_WAIT(2, &uempty[ustage], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 uint8_t* su = sU + ustage * C::USTAGE_BYTES;
@@ -304,9 +306,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-                const int64_t m = n - n0;
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t m = w.s, rt = w.rt;
                 const int b = (int)(m % NSB);
                 if (rt != cur_rt) {
                     if (!FD_WAIT(6, qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
@@ -327,7 +328,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     FD_SPAN_END(14);
                 }
                 // both issuers arrive at every row-tile end (qempty counts 2)
-                if ((n + 1 == n1) || (jt + 1 == n_jt)) ptx::umma_commit(qempty);
+                if (w.seg_last()) ptx::umma_commit(qempty);
                 if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
             }
             ptx::umma_commit(&done[q]);
@@ -351,9 +352,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             uint32_t uph = 0, ocount = 0;
             bool fresh = true;
             int gcnt = 0;
-            int64_t rt = n0 / n_jt, jt = n0 - rt * n_jt;
-            for (int64_t n = n0; n < n1; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-                const int64_t m = n - n0;
+            for (Walk w(sc, cta); !w.done(); w.next()) {
+                const int64_t m = w.s;
                 const int pb = (int)(m % NSB);
                 if (!FD_WAIT(3, &ufull[ustage], uph, abort, status, WAIT_LIMIT_NS)) break;
                 if (!FD_WAIT(4, &pfull[pb], (uint32_t)((m / NSB) & 1), abort, status, WAIT_LIMIT_NS)) break;
@@ -373,7 +373,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 ptx::umma_commit(&uempty[ustage]);
                 FD_SPAN_END(13);
                 if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
-                const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
+                const bool seg_last = w.seg_last();
                 if (seg_last || ++gcnt == ogroup) {     // end of an O group
                     ptx::umma_commit(&ofull[pb]);       // the group's reader: tile m's warpgroup
                     fresh = true;
@@ -397,15 +397,13 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-        const int64_t first_rt = n0 / n_jt;
         float* sacc = (float*)(base + C::ACC_OFF);
         uint32_t ogroups = 0, oread = 0;
         int gcnt = 0;
         bool seg_fresh = true;
         bool alive = true;
-        int64_t rt = first_rt, jt = n0 - first_rt * n_jt;
-        for (int64_t n = n0; n < n1 && alive; ++n, (++jt == n_jt ? (jt = 0, ++rt) : 0)) {
-            const int64_t m = n - n0;
+        for (Walk w(sc, cta); !w.done() && alive; w.next()) {
+            const int64_t m = w.s, rt = w.rt;
             const bool mine = (int)(m % NSB) == wg;
             if (mine) {
                 const int b = wg;
@@ -450,7 +448,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(&pfull[b]);
             }
-            const bool seg_last = (n + 1 == n1) || (jt + 1 == n_jt);
+            const bool seg_last = w.seg_last();
             const bool grp_end = seg_last || (++gcnt == ogroup);
             if (!grp_end) continue;
             gcnt = 0;
@@ -486,13 +484,12 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 if (lane == 0) ptx::mbar_arrive(oempty);
                 if (seg_last) {
                     const int64_t gi = rt * BM + row;
-                    const int64_t seg_first = (rt == first_rt) ? (n0 - rt * n_jt) : 0;
-                    const bool full = seg_first == 0 && jt == n_jt - 1;
+                    const bool full = w.seg_full();
                     if (gi < nq) {
                         for (int c = 0; c < rc; ++c) {
                             const double val = (double)sacc[c * BM + row] * (double)colscale[c];
                             if (full) store_out(ep, gi, c, val);
-                            else part[(((int64_t)cta * 2 + (rt == first_rt ? 0 : 1)) * BM + row) * RP + c] = val;
+                            else part[(((int64_t)cta * 2 + w.slot()) * BM + row) * RP + c] = val;
                         }
                     }
                 }
@@ -517,15 +514,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
 __global__ void tc_block_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, int rc, int rp,
                                       RowEpilogue ep) {
     const int64_t rt = blockIdx.x;
-    const int64_t lo = rt * sc.n_jt, hi = lo + sc.n_jt - 1;
-    auto owner = [&](int64_t n) {
-        int c = (int)(n * sc.grid / sc.units);
-        if (c >= sc.grid) c = sc.grid - 1;
-        while (c + 1 < sc.grid && sc.start(c + 1) <= n) ++c;
-        while (c > 0 && sc.start(c) > n) --c;
-        return c;
-    };
-    const int c_lo = owner(lo), c_hi = owner(hi);
+    int c_lo, c_hi;
+    cut_owners(sc, rt, &c_lo, &c_hi);
     if (c_lo == c_hi) return;
     for (int e = threadIdx.x; e < BM * rc; e += blockDim.x) {
         const int r = e / rc, col = e % rc;
@@ -533,10 +523,8 @@ __global__ void tc_block_fixup_kernel(const double* __restrict__ part, Sched sc,
         if (gi >= nq) continue;
         double sum = 0.0;
         for (int c = c_lo; c <= c_hi; ++c) {
-            const int64_t st = sc.start(c);
-            if (st == sc.start(c + 1)) continue;
-            const int slot = (st / sc.n_jt == rt) ? 0 : 1;
-            sum += part[(((int64_t)c * 2 + slot) * BM + r) * rp + col];
+            if (sc.start(c) == sc.start(c + 1)) continue;
+            sum += part[(((int64_t)c * 2 + cut_slot(sc, c, rt)) * BM + r) * rp + col];
         }
         store_out(ep, gi, col, sum);
     }
@@ -635,9 +623,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     FD_TRY(make_tile_map(&a.mu, ut, 2 * rp, ld, rp, true));   // U_hi^T rows then U_lo^T rows
     a.iqk = ptx::idesc_f32acc(tcb::BM, tcb::BN, f16);
     a.ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
-    a.sc.n_jt = cdiv(nk, tcb::BN);
-    a.sc.units = cdiv(nq, tcb::BM) * a.sc.n_jt;
-    a.sc.grid = (int)std::min<int64_t>(num_sms(), a.sc.units);
+    a.sc = tc::Sched::make(cdiv(nq, tcb::BM), cdiv(nk, tcb::BN), num_sms(), (size_t)nk * kd * 2);
     a.part = (double*)ws;
     a.colscale = colscale;
     a.rc = rc;

@@ -23,12 +23,101 @@ struct Geo {
     }
 };
 
+// Work split of the persistent kernels over (row tile, key tile) units.
+// First `full` whole row tiles per CTA, CTA c taking rows c, c + grid, ...:
+// every CTA starts each of these rows at key tile 0 at about the same time, so
+// the CTAs sweep K in near lockstep and a key tile is read from DRAM once per
+// sweep and then served from L2 (with CTAs at scattered key offsets, a K larger
+// than L2 is streamed from DRAM once per CTA).  The remaining row tiles
+// (fewer than grid) are cut into grid contiguous ranges of units; a row tile
+// cut between ranges leaves fp64 partials that the fix-up kernel sums in CTA
+// order (deterministic).
 struct Sched {
     int64_t n_jt;    // key tiles per row tile
-    int64_t units;   // n_rt * n_jt
+    int64_t units;   // units of the remainder region: (n_rt - full * grid) * n_jt
+    int64_t full;    // whole row tiles per CTA
     int grid;
-    __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }
+    __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }   // remainder range
+    __host__ __device__ int64_t rem_rt0() const { return full * grid; }
+    // schedule for n_rt row tiles of n_jt key tiles on at most `sms` CTAs; the
+    // lockstep rows only pay when the key operand does not stay in L2 anyway
+    // (measured: +17 % at 288 MB of keys, through lower DRAM power and higher
+    // clocks under the power cap; -3 % at 32 MB), so below `key_bytes` of
+    // 48 MB every unit goes to the contiguous ranges
+    static Sched make(int64_t n_rt, int64_t n_jt, int sms, size_t key_bytes) {
+        Sched sc;
+        sc.n_jt = n_jt;
+        const int64_t total = n_rt * n_jt;
+        sc.grid = (int)(total < sms ? total : sms);
+        const bool lockstep = key_bytes > ((size_t)48 << 20);
+        sc.full = (lockstep && n_rt >= sc.grid) ? n_rt / sc.grid : 0;
+        sc.units = (n_rt - sc.full * sc.grid) * n_jt;
+        return sc;
+    }
 };
+
+// One CTA's units in processing order (the same sequence in every role).
+struct Walk {
+    int64_t s = 0, steps, nfull, rt, jt, rem_first_rt, rem_u0;
+    int64_t n_jt, grid, rem_rt0;
+    __device__ Walk(const Sched& sc, int c) {
+        n_jt = sc.n_jt;
+        grid = sc.grid;
+        rem_rt0 = sc.rem_rt0();
+        nfull = sc.full * sc.n_jt;
+        rem_u0 = sc.start(c);
+        steps = nfull + sc.start(c + 1) - rem_u0;
+        rem_first_rt = rem_rt0 + rem_u0 / n_jt;
+        if (nfull > 0) {
+            rt = c;
+            jt = 0;
+        } else {
+            rt = rem_first_rt;
+            jt = rem_u0 - (rt - rem_rt0) * n_jt;
+        }
+    }
+    __device__ bool done() const { return s >= steps; }
+    __device__ void next() {
+        ++s;
+        if (s == nfull) {
+            rt = rem_first_rt;
+            jt = rem_u0 - (rt - rem_rt0) * n_jt;
+        } else if (++jt == n_jt) {
+            jt = 0;
+            rt += s < nfull ? grid : 1;
+        }
+    }
+    // last unit of this CTA's segment of row tile rt
+    __device__ bool seg_last() const { return jt + 1 == n_jt || s + 1 == steps; }
+    // the segment covers all key tiles of the row (then the output is final)
+    __device__ bool seg_full() const {
+        const bool starts_at_0 = s < nfull || rt != rem_first_rt || rem_u0 == (rt - rem_rt0) * n_jt;
+        return starts_at_0 && jt == n_jt - 1;
+    }
+    // partial-sum slot of a cut row: 0 = the first remainder row, 1 = the last
+    __device__ int slot() const { return rt == rem_first_rt ? 0 : 1; }
+};
+
+// Fix-up helper: the CTAs whose remainder ranges touch row tile rt
+// (c_lo == c_hi: the row was not cut; whole rows are never cut).
+__device__ inline void cut_owners(const Sched& sc, int64_t rt, int* c_lo, int* c_hi) {
+    *c_lo = *c_hi = 0;
+    if (rt < sc.rem_rt0()) return;
+    const int64_t lo = (rt - sc.rem_rt0()) * sc.n_jt, hi = lo + sc.n_jt - 1;
+    auto owner = [&](int64_t n) {
+        int c = (int)(n * sc.grid / sc.units);
+        if (c >= sc.grid) c = sc.grid - 1;
+        while (c + 1 < sc.grid && sc.start(c + 1) <= n) ++c;
+        while (c > 0 && sc.start(c) > n) --c;
+        return c;
+    };
+    *c_lo = owner(lo);
+    *c_hi = owner(hi);
+}
+// slot of CTA c's partial for row tile rt (c in [c_lo, c_hi], non-empty range)
+__device__ inline int cut_slot(const Sched& sc, int c, int64_t rt) {
+    return (sc.rem_rt0() + sc.start(c) / sc.n_jt == rt) ? 0 : 1;
+}
 
 // ---- exp2 of a pair of exponents --------------------------------------------
 // MUFU: two ex2.approx.ftz.  The exponent is <= 0 up to fp32 rounding of the

@@ -320,3 +320,22 @@ def test_block_path_no_drift_over_many_key_tiles(prec):
     for c, s in enumerate((1.0, -3.0)):
         err = float(torch.linalg.vector_norm(Y[:, c] - s * x) / torch.linalg.vector_norm(s * x))
         assert err <= 2e-5, (c, err)
+
+
+@pytest.mark.parametrize("r", [1, 3])
+def test_lockstep_schedule_large_keys(r):
+    """K operand > 48 MB (200k keys, d=128): whole row tiles in lockstep, then cut remainder rows.
+
+    40,000 query rows = 157 row tiles of 256 (r=1) / 313 of 128 (r>1): one or two whole rows per
+    CTA plus a remainder cut between CTAs; rows from both regions against the exact sum."""
+    from flashdiffusion_b200 import GaussianOperator, synthetic
+    X, beta = synthetic.tanh_manifold(n=200_000, d=128, seed=7)
+    Q = X[:40_000] + np.float32(0.01)
+    op = GaussianOperator(Q, X, beta, "f16")
+    rng = np.random.default_rng(8)
+    V = rng.standard_normal((X.shape[0], r))
+    out = op.apply(torch.from_numpy(V).cuda(), out_dtype=torch.float64).cpu().numpy()
+    rows = np.concatenate([rng.choice(37_888, 24, replace=False), 37_888 + rng.choice(40_000 - 37_888, 24, replace=False)])
+    ref = exact_apply(Q[rows], X, V, beta)
+    for c in range(r):
+        assert rel_l2(out[rows, c], ref[:, c]) <= TOL["f16"], c
