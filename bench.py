@@ -205,7 +205,8 @@ class ClockSampler:
 # DRAM bytes per launch of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum; the capture commands are in
 # the named profile summaries).
-TRAFFIC = {"c2": (70.3e6, "profiles/tc_kernel_c2_dmap_matvec.md")}
+TRAFFIC = {"c2": (69.3e6, "profiles/tc_kernel_c2_dmap_matvec.md"),
+           "c5r1": (22.58e9, "profiles/tc_kernel_c5r1_dmap_matvec.md")}
 
 
 def load_peaks():
@@ -409,11 +410,16 @@ def run_ours(args):
         cs = CpuSampler(Q, K, beta, r)
         if args.cpu_rows:
             cpu_rows = args.cpu_rows
-        else:   # calibrate, then size the sample to about 10 s of CPU work
-            cal = max(64, 8 * cs.procs)
-            _, dtc, _ = cs.sample(cal)
-            cpu_rows = int(min(nq, max(cal, cal * 10.0 / max(dtc, 1e-3))) // 64 * 64)
-        cpu_ev, cpu_dt, cpu_procs = cs.sample(cpu_rows)
+        else:   # grow the sample until it takes 5-20 s of CPU work (per-call overheads
+            # dominate small samples, so one small calibration overestimates the time)
+            cpu_rows = max(64, 8 * cs.procs)
+            while True:
+                cpu_ev, cpu_dt, cpu_procs = cs.sample(cpu_rows)
+                if cpu_dt >= 5.0 or cpu_rows >= nq:
+                    break
+                cpu_rows = int(min(nq, cpu_rows * min(16.0, max(2.0, 10.0 / max(cpu_dt, 1e-3)))))
+        if args.cpu_rows:
+            cpu_ev, cpu_dt, cpu_procs = cs.sample(cpu_rows)
         cs.close()
         cpu_baseline = {"value": cpu_ev, "unit": "evals/s", "cores": cpu_procs, "kind": "port",
                         "sample": f"{cpu_rows} seeded rows x all {nk} keys, r={r}: NumPy tile loop of the reference "
