@@ -162,7 +162,7 @@ simt_kernel(const float* __restrict__ qp, const float* __restrict__ qsq, int64_t
 // ---- r = 1: 128 x 128 tiles, 8 x 8 per thread, cp.async double buffering ------
 // Rows ty + 16a and columns tx + 16b of the tile belong to thread (ty, tx):
 // operands stay row-major in shared memory with a row pitch dpp = 4 x odd
-// floats, so the float2 reads of 16 lanes with consecutive tx hit distinct
+// floats, so the float4 reads of 16 lanes with consecutive tx hit distinct
 // bank groups and the query reads are broadcasts.  The next key tile (points,
 // squared norms, u) is copied by cp.async while the current one is computed;
 // rows past nk are zero-filled and masked.  One CTA per SM (up to 222 KB of
@@ -245,18 +245,20 @@ simt1_kernel(const float* __restrict__ qp, const float* __restrict__ qsq, int64_
         for (int a = 0; a < 8; ++a)
 #pragma unroll
             for (int b = 0; b < 8; ++b) dot[a][b] = 0.f;
-        for (int k = 0; k < dp; k += 2) {
-            float2 qv[8], kv[8];
+        for (int k = 0; k < dp; k += 4) {
+            float4 qv[8], kv[8];
 #pragma unroll
-            for (int a = 0; a < 8; ++a) qv[a] = *(const float2*)&Qs[(ty + 16 * a) * dpp + k];
+            for (int a = 0; a < 8; ++a) qv[a] = *(const float4*)&Qs[(ty + 16 * a) * dpp + k];
 #pragma unroll
-            for (int b = 0; b < 8; ++b) kv[b] = *(const float2*)&Kb[(tx + 16 * b) * dpp + k];
+            for (int b = 0; b < 8; ++b) kv[b] = *(const float4*)&Kb[(tx + 16 * b) * dpp + k];
 #pragma unroll
             for (int a = 0; a < 8; ++a)
 #pragma unroll
                 for (int b = 0; b < 8; ++b) {
                     dot[a][b] = fmaf(qv[a].x, kv[b].x, dot[a][b]);
                     dot[a][b] = fmaf(qv[a].y, kv[b].y, dot[a][b]);
+                    dot[a][b] = fmaf(qv[a].z, kv[b].z, dot[a][b]);
+                    dot[a][b] = fmaf(qv[a].w, kv[b].w, dot[a][b]);
                 }
         }
         const int64_t j0 = jt * TB;
