@@ -495,3 +495,30 @@ int read_and_clear_status(cudaStream_t s, int* status) {
 }
 
 }  // namespace fd
+
+namespace {
+// One bounded wait on an mbarrier that nothing arrives at: the failure path of
+// every pipeline wait in the kernels (limit, abort flag, status word), without
+// a fault.
+__global__ void wait_selftest_kernel(int* status, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        fd::ptx::mbar_init(&bar, 1);
+        abort_flag = 0;
+        fd::ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) fd::ptx::wait_bounded(&bar, 0, &abort_flag, status, limit_ns);
+}
+}  // namespace
+
+extern "C" int fd_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+    FD_CHECK_ARG(limit_ns >= 1000000 && limit_ns <= 2000000000, "fd_selftest_wait_timeout: limit %lld ns "
+                 "(1e6..2e9)", (long long)limit_ns);
+    int* status = nullptr;
+    FD_TRY(fd::status_word(&status));
+    wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(status, (uint64_t)limit_ns);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}

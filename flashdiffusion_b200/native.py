@@ -46,6 +46,7 @@ SIGNATURES = {
     "fd_dmap_weights": (_I, [_P, _L, _F, _P, _P]),
     "fd_dmap_rscale": (_I, [_P, _P, _L, _P, _P, _P]),
     "fd_set_block_options": (_I, [_I, _I]),
+    "fd_selftest_wait_timeout": (_I, [_L, _P]),
     "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
     "fd_pairwise_sqdist": (_I, [_P, _L, _I, _P, _P]),
     "fd_rope_windows": (_I, [_P, _L, _L, _P, _L, _L, _L, _I, _I, _I, _I, ctypes.c_double, _P, _I, _P, _P, _P,

@@ -205,6 +205,13 @@ int fd_rope_windows(const double* F, int64_t sT, int64_t sC, const double* pos, 
                     int D, int L, int window_mode, int c_w, double pos_scale, const double* freqs, int n_freqs,
                     const double* mu, const double* sigma, float* Y, void* stream);
 
+/* Failure-path self-test (no counterpart in the reference): launches one bounded
+ * device wait on a barrier that nothing arrives at, with a limit of limit_ns
+ * (1e6..2e9).  The wait gives up and records FD_ERR_TIMEOUT in the status word
+ * exactly as a stalled kernel pipeline would; the next fd_check_status on the
+ * stream returns FD_ERR_TIMEOUT and clears it, and the context stays usable. */
+int fd_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* Options of the block (r > 1) tensor-core path, process-wide, for the next
  * launches (no counterpart in the reference, whose GPU path has no block
  * product).  group_tiles: key tiles summed in one tensor-core accumulator

@@ -87,3 +87,41 @@ def test_row_gather_single_rank_is_identity():
     g = RowGather(10, 1)
     x = torch.arange(10.0)
     assert g(x) is x
+
+
+def _dropout_worker(rank, world, port, out_q):
+    import datetime
+    import time as _t
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    g = RowGather(600, world)
+    a, b = shard_rows(600, world, rank)
+    first = g(torch.full((b - a,), float(rank), dtype=torch.float64))   # one good product
+    if rank == 1:
+        out_q.put((rank, "left", float(first.sum())))
+        out_q.close()
+        out_q.join_thread()       # the message is out before the process goes
+        os._exit(0)               # leaves between products, with nothing in flight
+    t0 = _t.perf_counter()
+    try:
+        g(torch.zeros(b - a, dtype=torch.float64))
+        out_q.put((rank, "no error", _t.perf_counter() - t0))
+    except Exception as e:    # the collective ends with an error instead of hanging
+        out_q.put((rank, type(e).__name__, _t.perf_counter() - t0))
+
+
+def test_rank_that_leaves_is_detected_by_the_next_gather():
+    """Failure detection on the host: a rank exits between products; the other rank's next
+    all-gather ends with an error within the process-group timeout instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dropout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (what, val)) for r, what, val in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][0] == "left"
+    assert res[0][0] != "no error", res[0]
+    assert res[0][1] < 60.0

@@ -339,3 +339,19 @@ def test_lockstep_schedule_large_keys(r):
     ref = exact_apply(Q[rows], X, V, beta)
     for c in range(r):
         assert rel_l2(out[rows, c], ref[:, c]) <= TOL["f16"], c
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    """A device wait that nothing releases gives up after its limit, the status word says
+    FD_ERR_TIMEOUT once, and later launches on the same context work."""
+    from flashdiffusion_b200 import native, FlashDiffusion
+    dev = native.require_device()
+    lib = native.load()
+    native.check(lib.fd_selftest_wait_timeout(50_000_000, native._stream(dev)))
+    torch.cuda.synchronize()
+    assert lib.fd_check_status(native._stream(dev)) == native.FD_ERR_TIMEOUT
+    assert lib.fd_check_status(native._stream(dev)) == native.FD_OK
+    X = np.random.default_rng(0).standard_normal((500, 8)).astype(np.float32)
+    v = np.random.default_rng(1).standard_normal(500)
+    out = FlashDiffusion(X, X, v, 0.1, precision="f16")
+    assert rel_l2(out, O.flash_diffusion(X, X, v, 0.1)) <= TOL["f16"]
