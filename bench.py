@@ -342,9 +342,7 @@ def run_ours(args):
     # their rounding floor, then fp32-class tiles with an fp64 Rayleigh-Ritz),
     # device fp64 basis, outside the timed region
     lanczos = None
-    # (c5r1 is the matvec target only: configuration 5's eigenproblem is the
-    # k = 32 LOBPCG of --config c5 --lobpcg)
-    if not args.no_lanczos and cfg["mode"] in ("dmap", "doob") and r == 1 and args.config != "c5r1":
+    if not args.no_lanczos and cfg["mode"] in ("dmap", "doob") and r == 1:
         from flashdiffusion_b200.eigensolver import ramp_eigsh
         # configuration 2: k = 16 of the DMAP operator; configuration 4: k = 8 of the
         # Doob operator, through its symmetric similar form

@@ -110,7 +110,9 @@ int fd_pack_operand(const void* X, int dtype, int64_t n, int d, const float* shi
     FD_CHECK_ARG(valid_tile(tile), "bad tile %d", tile);
     FD_CHECK_ARG(side == FD_SIDE_QUERY || side == FD_SIDE_KEY, "bad side %d", side);
     FD_CHECK_ARG(beta > 0.f, "beta must be positive (got %g)", (double)beta);
-    FD_CHECK_ARG(tile != FD_TILE_F16X3 || d <= 66, "FD_TILE_F16X3 supports d <= 66 (got %d)", d);
+    FD_CHECK_ARG(kd_tile(tile, d) <= 416 || tile == FD_TILE_F32,
+                 "tensor-core tiles support operand rows of up to 416 columns (d <= %d for this tile)",
+                 tile == FD_TILE_F16X3 ? 136 : 410);
     FD_CHECK_ARG(n == 0 || (X && operand), "null pointer");
     FD_CHECK_ARG(((uintptr_t)operand & 255) == 0, "operand must be 256-byte aligned");
     return launch_pack(X, dtype, n, d, shift, beta, side, tile, operand, (cudaStream_t)stream);
@@ -141,7 +143,11 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
     if (nq == 0) return FD_OK;
 
     // (the workspace query is sized for 64 block columns, an upper bound for any d)
-    const int cpl = (is_tc_tile(tile) && r > 1) ? block_max_cols(d) : cols_per_launch(tile, r);
+    // block tensor-core path for r > 1 up to 208 operand columns; wider operands
+    // (the 128-row streaming kernel) take one column per launch
+    const bool wide = is_tc_tile(tile) && kd_tile(tile, d) > 208;
+    const bool block = is_tc_tile(tile) && r > 1 && !wide;
+    const int cpl = block ? block_max_cols(d) : (wide ? 1 : cols_per_launch(tile, r));
     const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
     uint8_t* ws = (uint8_t*)workspace;
     float* u = (float*)ws;
@@ -151,7 +157,7 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
         const int rc = std::min(cpl, r - c0);
         RowEpilogue ep{row_scale, row_div, out, out_dtype, (int64_t)r, c0};
         if (nk == 0) { FD_TRY(launch_zero_rows(nq, rc, ep, s)); continue; }
-        if (is_tc_tile(tile) && r > 1) {
+        if (block) {
             const int rp = block_rp(rc);
             __half* ut = (__half*)ws;
             float* colscale = (float*)(ws + align256(sizeof(__half) * 2 * (size_t)nk_pad * rp));

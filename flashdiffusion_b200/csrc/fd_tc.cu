@@ -323,6 +323,287 @@ __global__ void tc_fixup_kernel(const double* __restrict__ part, Sched sc, int64
     }
 }
 
+
+// ---- wide operands: kd in (208, 416] -------------------------------------------
+// The fp32-class split operands (FD_TILE_F16X3, kd = 3d + 6 rounded) of
+// d = 68..136, and 16-bit operands of d > 202, do not fit the kernel above
+// (its 256-row query tile plus whole-key-tile stages would need up to 310 KB
+// of shared memory).  tcw_kernel keeps a 128-row query tile resident and
+// streams each key tile as its 64-column boxes through a ring of 16 KB slots,
+// so the Q.K^T chain of a tile waits box by box; four TMEM S buffers (all 512
+// columns) let four epilogue warpgroups (tile m -> warpgroup m mod 4) overlap
+// the chain.  Warp roles (18 warps): 0-15 epilogue, 16 TMA producer (query
+// tile once per row tile, key boxes, u through a 4-deep ring), 17 the MMA
+// issuer.  The tensor pipe bounds it: 2 kd flops per evaluation.
+namespace w {
+constexpr int BM = 128;                 // query rows per tile = TMEM lanes
+constexpr int BN = 128;                 // keys per tile
+constexpr int NSB = 4;                  // S buffers = epilogue warpgroups
+constexpr int TMA_WARP = 16;
+constexpr int MMA_WARP = 17;
+constexpr int NTHREADS = 18 * 32;
+constexpr uint32_t SLOT_BYTES = BN * 128;   // one 64-column box of a key tile
+
+template <int KF, int NW>
+struct Cfg {
+    static constexpr int NB = KF + (NW ? 1 : 0);                      // boxes per key tile
+    static constexpr uint32_t Q_BYTES = BM * (KF * 128 + NW * 2);
+    static constexpr uint32_t NARROW_BYTES = BN * NW * 2;
+    static constexpr int SLOTS_RAW = (int)((221u * 1024u - Q_BYTES - URING * U_BYTES) / SLOT_BYTES);
+    static constexpr int SLOTS = SLOTS_RAW > 12 ? 12 : SLOTS_RAW;
+    static_assert(SLOTS >= 3, "shared memory budget");
+    static constexpr uint32_t RING_OFF = (Q_BYTES + 1023) & ~1023u;
+    static constexpr uint32_t U_OFF = RING_OFF + SLOTS * SLOT_BYTES;
+    static constexpr uint32_t BAR_OFF = U_OFF + URING * U_BYTES;
+    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4], rfull, rempty, done
+    static constexpr int NBARS = 2 * SLOTS + 2 * URING + 2 + 2 * NSB + 3;
+    static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
+    static constexpr uint32_t RED_OFF = (MISC_OFF + 16 + 15) & ~15u;
+    static constexpr uint32_t SMEM_BYTES = RED_OFF + (NSB - 1) * BM * 8;
+    static constexpr uint32_t SMEM_ALLOC = SMEM_BYTES + 1024;
+    static_assert(SMEM_ALLOC <= 227u * 1024u, "shared memory budget");
+};
+}  // namespace w
+
+template <int KF, int NW, int EMU>
+__global__ void __launch_bounds__(w::NTHREADS, 1)
+tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+           const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
+           const float* __restrict__ u, int64_t nq, uint32_t idesc, Sched sc, RowEpilogue ep,
+           double* __restrict__ part, int* __restrict__ status) {
+    using C = w::Cfg<KF, NW>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = base;
+    uint8_t* sR = base + C::RING_OFF;
+    float* sU = (float*)(base + C::U_OFF);
+    uint64_t* bars = (uint64_t*)(base + C::BAR_OFF);
+    uint64_t* kfull = bars;
+    uint64_t* kempty = kfull + C::SLOTS;
+    uint64_t* ufull = kempty + C::SLOTS;
+    uint64_t* uempty = ufull + URING;
+    uint64_t* qfull = uempty + URING;
+    uint64_t* qempty = qfull + 1;
+    uint64_t* sfull = qempty + 1;
+    uint64_t* sempty = sfull + w::NSB;
+    uint64_t* rfull = sempty + w::NSB;
+    uint64_t* rempty = rfull + 1;
+    uint64_t* done = rempty + 1;
+    uint32_t* tmem_slot = (uint32_t*)(base + C::MISC_OFF);
+    volatile int* abort = (volatile int*)(base + C::MISC_OFF + 4);
+    double* red = (double*)(base + C::RED_OFF);   // [NSB - 1][BM]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int cta = blockIdx.x;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < C::SLOTS; ++i) {
+            ptx::mbar_init(&kfull[i], 1);
+            ptx::mbar_init(&kempty[i], 1);
+        }
+        for (int i = 0; i < URING; ++i) {
+            ptx::mbar_init(&ufull[i], 1);
+            ptx::mbar_init(&uempty[i], 4);      // the 4 warps of the warpgroup of tile m = i (mod 4)
+        }
+        ptx::mbar_init(qfull, 1);
+        ptx::mbar_init(qempty, 1);
+        for (int i = 0; i < w::NSB; ++i) {
+            ptx::mbar_init(&sfull[i], 1);
+            ptx::mbar_init(&sempty[i], 4);
+        }
+        ptx::mbar_init(rfull, (w::NSB - 1) * w::BM);   // every thread of warpgroups 1-3
+        ptx::mbar_init(rempty, w::BM);                 // every thread of warpgroup 0
+        ptx::mbar_init(done, 1);
+        *abort = 0;
+        ptx::fence_mbar_init();
+    }
+    if (warp == w::MMA_WARP) {
+        ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+        ptx::tmem_relinquish();
+    }
+    if (warp == w::TMA_WARP && lane == 0) {
+        ptx::prefetch_tmap(&tmq);
+        ptx::prefetch_tmap(&tmk);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == w::TMA_WARP) {
+        if (lane == 0) {
+            int slot = 0;
+            uint32_t kph = 0, qcount = 0;
+            int64_t cur_rt = -1;
+            for (Walk wk(sc, cta); !wk.done(); wk.next()) {
+                const int64_t m = wk.s, rt = wk.rt, jt = wk.jt;
+                if (rt != cur_rt) {
+                    if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    ptx::mbar_expect_tx(qfull, C::Q_BYTES);
+                    for (int kb = 0; kb < KF; ++kb)
+                        ptx::tma_load_2d(sQ + kb * w::BM * 128, &tmq, qfull, kb * 64, (int)(rt * w::BM));
+                    if (NW) ptx::tma_load_2d(sQ + KF * w::BM * 128, &tmq_n, qfull, KF * 64, (int)(rt * w::BM));
+                    cur_rt = rt;
+                    ++qcount;
+                }
+                bool ok = true;
+                for (int kb = 0; kb < C::NB; ++kb) {
+                    if (!ptx::wait_bounded(&kempty[slot], kph ^ 1, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    uint8_t* dst = sR + slot * w::SLOT_BYTES;
+                    if (kb < KF) {
+                        ptx::mbar_expect_tx(&kfull[slot], w::SLOT_BYTES);
+                        ptx::tma_load_2d(dst, &tmk, &kfull[slot], kb * 64, (int)(jt * w::BN));
+                    } else {
+                        ptx::mbar_expect_tx(&kfull[slot], C::NARROW_BYTES);
+                        ptx::tma_load_2d(dst, &tmk_n, &kfull[slot], KF * 64, (int)(jt * w::BN));
+                    }
+                    if (++slot == C::SLOTS) { slot = 0; kph ^= 1; }
+                }
+                if (!ok) break;
+                const int us = (int)(m & (URING - 1));
+                const uint32_t uph = (uint32_t)((m / URING) & 1);
+                if (!ptx::wait_bounded(&uempty[us], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                ptx::mbar_expect_tx(&ufull[us], U_BYTES);
+                ptx::bulk_load(sU + us * w::BN, u + jt * w::BN, U_BYTES, &ufull[us]);
+            }
+        }
+    } else if (warp == w::MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t q_base = ptx::smem_u32(sQ), r_base = ptx::smem_u32(sR);
+            int slot = 0;
+            uint32_t kph = 0, qcount = 0;
+            int64_t cur_rt = -1;
+            for (Walk wk(sc, cta); !wk.done(); wk.next()) {
+                const int64_t m = wk.s, rt = wk.rt;
+                const int b = (int)(m % w::NSB);
+                if (rt != cur_rt) {
+                    if (!ptx::wait_bounded(qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
+                    ++qcount;
+                    cur_rt = rt;
+                }
+                if (!ptx::wait_bounded(&sempty[b], (uint32_t)(((m / w::NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
+                bool ok = true;
+                for (int kb = 0; kb < C::NB; ++kb) {
+                    if (!ptx::wait_bounded(&kfull[slot], kph, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    ptx::tc_fence_after();
+                    const uint32_t ka = r_base + slot * w::SLOT_BYTES;
+                    if (kb < KF) {
+                        const uint32_t qa = q_base + kb * w::BM * 128;
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks)
+                            ptx::umma_ss(tmem + b * w::BN, ptx::sw128_kmajor_desc(qa + ks * 32),
+                                         ptx::sw128_kmajor_desc(ka + ks * 32), idesc, (kb | ks) ? 1u : 0u);
+                    } else {
+                        const uint32_t qa = q_base + KF * w::BM * 128;
+#pragma unroll
+                        for (int ks = 0; ks < NW / 16; ++ks) {
+                            const uint64_t dq = NW == 32 ? ptx::sw64_kmajor_desc(qa + ks * 32) : ptx::sw32_kmajor_desc(qa + ks * 32);
+                            const uint64_t dk = NW == 32 ? ptx::sw64_kmajor_desc(ka + ks * 32) : ptx::sw32_kmajor_desc(ka + ks * 32);
+                            ptx::umma_ss(tmem + b * w::BN, dq, dk, idesc, 1u);
+                        }
+                    }
+                    ptx::umma_commit(&kempty[slot]);
+                    if (++slot == C::SLOTS) { slot = 0; kph ^= 1; }
+                }
+                if (!ok) break;
+                ptx::umma_commit(&sfull[b]);
+                if (wk.seg_last()) ptx::umma_commit(qempty);
+            }
+            ptx::umma_commit(done);
+            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
+        }
+    } else if (warp < 16) {
+        // ---- epilogue: warpgroup wg owns S buffer wg and the tiles m = wg (mod 4)
+        const int wg = warp >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+        double acc = 0.0;
+        uint32_t segs = 0;
+        bool alive = true;
+        for (Walk wk(sc, cta); !wk.done() && alive; wk.next()) {
+            const int64_t m = wk.s, rt = wk.rt;
+            if ((int)(m % w::NSB) == wg) {
+                const uint32_t use = (uint32_t)(m / w::NSB);
+                const int us = (int)(m & (URING - 1));
+                if (!ptx::wait_bounded(&ufull[us], (uint32_t)((m / URING) & 1), abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                if (!ptx::wait_bounded(&sfull[wg], use & 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                ptx::tc_fence_after();
+                const float* ut = sU + us * w::BN;
+                uint64_t acc_a = 0, acc_b = 0;
+                uint32_t va[16], vb[16];
+                const uint32_t tb = t_lane + wg * w::BN;
+                ptx::tmem_ld16(tb, va);
+                ptx::tmem_wait_ld16(va);
+#pragma unroll 1
+                for (int c = 0; c < w::BN / 16; c += 2) {
+                    ptx::tmem_ld16(tb + (c + 1) * 16, vb);
+                    chunk16_r1<EMU>(va, ut + c * 16, acc_a, acc_b);
+                    ptx::tmem_wait_ld16(vb);
+                    if (c + 2 < w::BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
+                    chunk16_r1<EMU>(vb, ut + (c + 1) * 16, acc_a, acc_b);
+                    if (c + 2 < w::BN / 16) ptx::tmem_wait_ld16(va);
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::mbar_arrive(&sempty[wg]);
+                    ptx::mbar_arrive(&uempty[us]);
+                }
+                uint32_t a0, a1, b0, b1;
+                ptx::unpack2(acc_a, a0, a1);
+                ptx::unpack2(acc_b, b0, b1);
+                acc += (double)((__uint_as_float(a0) + __uint_as_float(a1)) + (__uint_as_float(b0) + __uint_as_float(b1)));
+            }
+            if (wk.seg_last()) {
+                // the four warpgroups' partial row sums meet in warpgroup 0
+                const uint32_t ph = segs & 1;
+                if (wg > 0) {
+                    if (!ptx::wait_bounded(rempty, ph ^ 1, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    red[(wg - 1) * w::BM + row] = acc;
+                    ptx::mbar_arrive(rfull);
+                } else {
+                    if (!ptx::wait_bounded(rfull, ph, abort, status, WAIT_LIMIT_NS)) { alive = false; break; }
+                    const double tot = acc + red[row] + red[w::BM + row] + red[2 * w::BM + row];
+                    ptx::mbar_arrive(rempty);
+                    const int64_t gi = rt * w::BM + row;
+                    if (gi < nq) {
+                        if (wk.seg_full()) store_out(ep, gi, 0, tot);
+                        else part[((int64_t)cta * 2 + wk.slot()) * w::BM + row] = tot;
+                    }
+                }
+                acc = 0.0;
+                ++segs;
+            }
+        }
+        ptx::tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == w::MMA_WARP) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// Fix-up of the wide kernel: 128-row tiles.
+__global__ void tcw_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, RowEpilogue ep) {
+    const int64_t rt = blockIdx.x;
+    int c_lo, c_hi;
+    cut_owners(sc, rt, &c_lo, &c_hi);
+    if (c_lo == c_hi) return;
+    for (int r = threadIdx.x; r < w::BM; r += blockDim.x) {
+        const int64_t gi = rt * w::BM + r;
+        if (gi >= nq) continue;
+        double sum = 0.0;
+        for (int c = c_lo; c <= c_hi; ++c) {
+            if (sc.start(c) == sc.start(c + 1)) continue;
+            sum += part[((int64_t)c * 2 + cut_slot(sc, c, rt)) * w::BM + r];
+        }
+        store_out(ep, gi, 0, sum);
+    }
+}
+
 }  // namespace tc
 
 // ---- host side -----------------------------------------------------------------
@@ -430,6 +711,67 @@ static int launch_tc_emu(const TcArgs& a, int emu, cudaStream_t s) {
     }
 }
 
+template <int KF, int NW, int EMU>
+static int launch_tcw_kb(const TcArgs& a, cudaStream_t s) {
+    using C = tc::w::Cfg<KF, NW>;
+    FD_CUDA_TRY(cudaFuncSetAttribute(tc::tcw_kernel<KF, NW, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)C::SMEM_ALLOC));
+    int* status = nullptr;
+    FD_TRY(status_word(&status));
+    tc::tcw_kernel<KF, NW, EMU><<<a.sc.grid, tc::w::NTHREADS, C::SMEM_ALLOC, s>>>(
+        a.mq, a.mk, a.mqn, a.mkn, a.u, a.nq, a.idesc, a.sc, a.ep, a.part, status);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+template <int KF, int NW>
+static int launch_tcw_emu(const TcArgs& a, int emu, cudaStream_t s) {
+    return emu ? launch_tcw_kb<KF, NW, 4>(a, s) : launch_tcw_kb<KF, NW, 0>(a, s);
+}
+
+// Operand rows of 224..416 columns (fp32-class tiles of d = 68..136; 16-bit
+// tiles of d = 203..410): 128-row query tiles, key tiles streamed by box.
+static int launch_tc_wide(const void* qop, int64_t nq, const void* kop, int64_t nk, int kd, int tile,
+                          const void* rhs, const RowEpilogue& ep, void* ws, size_t ws_bytes, cudaStream_t s) {
+    int kf = 0, nw = 0;
+    split_kd(kd, &kf, &nw);
+    const size_t need = tc_workspace_bytes(nq, nk, 1);
+    if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "16-bit tile path: workspace %zu B < %zu B", ws_bytes, need);
+    TcArgs a;
+    const bool f16 = tile != FD_TILE_BF16;
+    FD_TRY(make_tile_map(&a.mq, qop, nq, kd, tc::w::BM, f16));
+    FD_TRY(make_tile_map(&a.mk, kop, nk, kd, tc::w::BN, f16));
+    a.mqn = a.mq;
+    a.mkn = a.mk;
+    if (nw) {
+        FD_TRY(make_tile_map(&a.mqn, qop, nq, kd, tc::w::BM, f16, nw));
+        FD_TRY(make_tile_map(&a.mkn, kop, nk, kd, tc::w::BN, f16, nw));
+    }
+    a.idesc = ptx::idesc_f32acc(tc::w::BM, tc::w::BN, f16);
+    a.sc = tc::Sched::make(cdiv(nq, tc::w::BM), cdiv(nk, tc::w::BN), num_sms(), (size_t)nk * kd * 2);
+    a.part = (double*)ws;
+    a.u = (const float*)rhs;
+    a.nq = nq;
+    a.ep = ep;
+    const int emu = exp2_fma_cols(tile) ? 1 : 0;
+    switch (kf * 100 + nw) {
+        case 332: FD_TRY((launch_tcw_emu<3, 32>(a, emu, s))); break;
+        case 400: FD_TRY((launch_tcw_emu<4, 0>(a, emu, s))); break;
+        case 416: FD_TRY((launch_tcw_emu<4, 16>(a, emu, s))); break;
+        case 432: FD_TRY((launch_tcw_emu<4, 32>(a, emu, s))); break;
+        case 500: FD_TRY((launch_tcw_emu<5, 0>(a, emu, s))); break;
+        case 516: FD_TRY((launch_tcw_emu<5, 16>(a, emu, s))); break;
+        case 532: FD_TRY((launch_tcw_emu<5, 32>(a, emu, s))); break;
+        case 600: FD_TRY((launch_tcw_emu<6, 0>(a, emu, s))); break;
+        case 616: FD_TRY((launch_tcw_emu<6, 16>(a, emu, s))); break;
+        case 632: FD_TRY((launch_tcw_emu<6, 32>(a, emu, s))); break;
+        default: return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: no kernel for kd=%d", kd);
+    }
+    tc::tcw_fixup_kernel<<<(unsigned)cdiv(nq, tc::w::BM), 256, 0, s>>>(a.part, a.sc, nq, ep);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
 int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile,
               const void* rhs, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes, cudaStream_t s) {
     if (nq == 0) return FD_OK;
@@ -438,7 +780,8 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     const int kd = kd_tile(tile, d);
     int kf = 0, nw = 0;
     split_kd(kd, &kf, &nw);
-    if (kd > 208) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 208)", kd);
+    if (kd > 416) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 416)", kd);
+    if (kd > 208) return launch_tc_wide(qop, nq, kop, nk, kd, tile, rhs, ep, ws, ws_bytes, s);
     const size_t need = tc_workspace_bytes(nq, nk, rc);
     if (ws_bytes < need) return set_error(FD_ERR_WORKSPACE, "16-bit tile path: workspace %zu B < %zu B", ws_bytes, need);
     TcArgs a;

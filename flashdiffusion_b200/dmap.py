@@ -111,7 +111,7 @@ class DiffusionMap:
         t0 = time.perf_counter()
         if self.precision == "ramp":
             def hi():
-                # fp32-class tensor-core tiles (split operands) when d <= 66, else fp32 SIMT tiles
+                # fp32-class tensor-core tiles (split operands) when d <= 136, else fp32 SIMT tiles
                 self._hi_state = self._state("f16x3")
                 return self._hi_state
             vals, vecs, info = ramp_eigsh(self._cuda_state, hi, N, k, tol=tol,

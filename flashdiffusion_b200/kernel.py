@@ -119,7 +119,7 @@ class GaussianOperator:
         self.nq, self.d = Qd.shape
         self.nk = Kd.shape[0]
         self.shift = native.mean_rows(Kd) if shift is None else shift
-        if self.tile == native.TILE_F16X3 and self.d > 66:
+        if self.tile == native.TILE_F16X3 and self.d > 136:
             self.tile, self.precision = native.TILE_F32, "fp32"     # split operand rows would not fit
         if self.tile in (native.TILE_F16, native.TILE_F16X3):
             # fp16 operands unless some packed value would leave the fp16 range

@@ -56,7 +56,7 @@ extern "C" {
                            records FD_ERR_RANGE in the status word when a row would overflow */
 #define FD_TILE_F16X3 3 /* tcgen05 tiles of fp32-class accuracy (rel. L2 <= 1e-5): each
                            coordinate split into fp16 hi + lo and three products
-                           (hi.hi + hi.lo + lo.hi) per pair; d <= 66 */
+                           (hi.hi + hi.lo + lo.hi) per pair; d <= 136 */
 
 /* operand side for fd_pack_operand */
 #define FD_SIDE_QUERY 0

@@ -355,3 +355,37 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     v = np.random.default_rng(1).standard_normal(500)
     out = FlashDiffusion(X, X, v, 0.1, precision="f16")
     assert rel_l2(out, O.flash_diffusion(X, X, v, 0.1)) <= TOL["f16"]
+
+
+@pytest.mark.parametrize("prec,d,nq,nk,r", [("f16x3", 128, 3000, 20_000, 1), ("f16x3", 70, 2000, 9_000, 1),
+                                           ("f16x3", 100, 700, 3_001, 3), ("f16x3", 136, 257, 1_100, 1),
+                                           ("f16", 300, 1000, 5_000, 1), ("f16", 210, 300, 2_000, 2)])
+def test_wide_operands_vs_exact(prec, d, nq, nk, r):
+    """Operand rows of 224..416 columns (fp32-class tiles of d = 68..136, 16-bit tiles of d > 202):
+    the 128-row streaming kernel (r > 1 one column per launch) against the exact fp64 sum."""
+    from flashdiffusion_b200 import GaussianOperator
+    rng = np.random.default_rng(nq + nk + d + r)
+    K = rng.standard_normal((nk, d)).astype(np.float32)
+    Q = K[rng.integers(0, nk, nq)] + 0.1 * rng.standard_normal((nq, d)).astype(np.float32)
+    beta = 1.0 / (2.0 * d)
+    op = GaussianOperator(Q, K, beta, prec)
+    assert op.precision == prec
+    V = rng.standard_normal((nk, r))
+    out = op.apply(torch.from_numpy(V).cuda(), out_dtype=torch.float64).cpu().numpy()
+    rows = rng.choice(nq, min(nq, 200), replace=False)
+    ref = exact_apply(Q[rows], K, V, beta)
+    tol = 1e-5 if prec == "f16x3" else TOL[prec]
+    for c in range(r):
+        assert rel_l2(out[rows, c], ref[:, c]) <= tol, c
+
+
+def test_wide_f16x3_lockstep_c5_shape():
+    """fp32-class tiles at the configuration-5 dimension (d=128) with a key operand of 160 MB
+    (lockstep schedule): rows from the whole-row and the cut-remainder regions."""
+    from flashdiffusion_b200 import GaussianOperator, synthetic
+    X, beta = synthetic.tanh_manifold(n=200_000, d=128, seed=11)
+    op = GaussianOperator(X[:60_000], X, beta, "f16x3")
+    v = np.random.default_rng(12).standard_normal(X.shape[0])
+    out = op.apply(torch.from_numpy(v).cuda(), out_dtype=torch.float64)[:, 0].cpu().numpy()
+    rows = np.concatenate([np.arange(0, 60_000, 1000), np.arange(56_832, 60_000, 97)])
+    assert rel_l2(out[rows], exact_apply(X[rows], X, v[:, None], beta)[:, 0]) <= 1e-5
