@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--lobpcg", action="store_true", help="block configurations: time LOBPCG to k = r eigenpairs")
     p.add_argument("--lobpcg-tol", type=float, default=1e-3)
     p.add_argument("--lobpcg-tol2", type=float, default=1e-5)
+    p.add_argument("--tiles", default="f16", choices=["f16", "bf16", "f16x3", "fp32"],
+                   help="tile precision of the timed operator (default the 16-bit fp16 tiles)")
     a = p.parse_args()
     if a.n:
         for c in CONFIGS.values():
@@ -273,7 +275,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    op = ShardedOperator(Qd, Kd, beta, 0.5, "f16", mode=cfg["mode"], h=hd)
+    op = ShardedOperator(Qd, Kd, beta, 0.5, args.tiles, mode=cfg["mode"], h=hd)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -425,10 +427,10 @@ def run_ours(args):
     line = {
         "metric": "kernel evals/sec per matvec (N^2/t)", "value": value, "unit": "evals/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 tiles, f32 accumulate",
+        "scaling": "strong", "vs_baseline": None, "dtype": f"{args.tiles} tiles, f32 accumulate",
         "data": "synthetic (seeded generator)",
         "config": {"workload": cfg["workload"], "n_q": nq, "n_k": nk, "d": d, "r": r, "beta": beta,
-                   "mode": cfg["mode"], "tiles": "f16 tcgen05", "parallelism": f"row-shard x{world}, NCCL all-gather",
+                   "mode": cfg["mode"], "tiles": f"{op.op.precision} tcgen05" if op.op.precision != "fp32" else "fp32 SIMT", "parallelism": f"row-shard x{world}, NCCL all-gather",
                    "l2": "flushed between steps (256 MB write)"},
         "roofline": {"bound": "mufu" if mufu_peak <= tensor_peak_evals else "tensor", "achieved": kern_evals,
                      "peak": peak_evals, "unit": "evals/s", "frac": kern_evals / peak_evals,
