@@ -10,7 +10,7 @@
 // columns) -> packed f32x2 FMA with u_j (staged in shared memory by TMA).
 //
 // CTA = 256 query rows (two 128-row subtiles sharing every key tile) x
-// stream of 128-row key tiles.  Warp roles (18 warps):
+// stream of 128-row key tiles.  Warp roles (19 warps):
 //   warps 0-15  four epilogue warpgroups (subtile s, parity p): WG(s,p) owns the
 //               TMEM S buffer 2s+p and the key tiles of parity p of subtile s
 //   warp  16    TMA producer: query tile once per row tile, key tiles through
