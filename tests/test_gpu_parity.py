@@ -389,3 +389,31 @@ def test_wide_f16x3_lockstep_c5_shape():
     out = op.apply(torch.from_numpy(v).cuda(), out_dtype=torch.float64)[:, 0].cpu().numpy()
     rows = np.concatenate([np.arange(0, 60_000, 1000), np.arange(56_832, 60_000, 97)])
     assert rel_l2(out[rows], exact_apply(X[rows], X, v[:, None], beta)[:, 0]) <= 1e-5
+
+
+def test_c5_full_size_properties():
+    """Configuration 5 at its 1M-point size (d=128), through properties that do not need an
+    O(N^2) reference: the exact eigenvector sqrt(D_alpha) (eigenvalue 1), the symmetry of M,
+    and a seeded row subset against the exact fp64 sum over all 1M keys."""
+    from flashdiffusion_b200 import GaussianOperator, synthetic
+    from flashdiffusion_b200.kernel_cuda_sm100 import normalise
+    X, beta = synthetic.tanh_manifold(n=1_000_000, d=128, seed=0)
+    op = GaussianOperator(X, None, beta, "f16")
+    _, Da, rs = normalise(op, 0.5)
+    M = lambda v: op.apply(v[:, None], col_scale=rs, row_scale=rs, out_dtype=torch.float64)[:, 0]
+    x = torch.sqrt(Da.double())
+    assert float(torch.linalg.vector_norm(M(x) - x) / torch.linalg.vector_norm(x)) <= 1e-6
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(X.shape[0], dtype=torch.float64, device="cuda", generator=g)
+    b = torch.randn(X.shape[0], dtype=torch.float64, device="cuda", generator=g)
+    Ma, Mb = M(a), M(b)
+    assert abs(float(a @ Mb - b @ Ma)) <= 1e-4 * float(torch.linalg.vector_norm(a) * torch.linalg.vector_norm(Mb))
+    v = np.random.default_rng(4).standard_normal(X.shape[0])
+    out = op.apply(torch.from_numpy(v).cuda(), out_dtype=torch.float64)[:, 0].cpu().numpy()
+    rows = np.random.default_rng(5).choice(X.shape[0], 12, replace=False)
+    ref = np.zeros(len(rows))
+    for c0 in range(0, X.shape[0], 250_000):   # exact fp64 sums, 250k keys at a time
+        Kc = X[c0:c0 + 250_000].astype(np.float64)
+        for i, r in enumerate(rows):
+            ref[i] += np.exp(-beta * ((Kc - X[r].astype(np.float64)) ** 2).sum(1)) @ v[c0:c0 + 250_000]
+    assert rel_l2(out[rows], ref) <= TOL["f16"]
