@@ -417,3 +417,38 @@ def test_c5_full_size_properties():
         for i, r in enumerate(rows):
             ref[i] += np.exp(-beta * ((Kc - X[r].astype(np.float64)) ** 2).sum(1)) @ v[c0:c0 + 250_000]
     assert rel_l2(out[rows], ref) <= TOL["f16"]
+
+
+def _exact_rows(Qrows, K, u, beta, chunk=250_000):
+    """Exact fp64 sum_j exp(-beta |q_i - k_j|^2) u_j for a few rows, keys in chunks."""
+    ref = np.zeros(len(Qrows))
+    for c0 in range(0, K.shape[0], chunk):
+        Kc = K[c0:c0 + chunk].astype(np.float64)
+        for i, q in enumerate(Qrows):
+            ref[i] += np.exp(-beta * ((Kc - np.asarray(q, np.float64)) ** 2).sum(1)) @ u[c0:c0 + chunk]
+    return ref
+
+
+def test_c3_c4_full_size_row_subsets():
+    """Configurations 3 (AMAP, 500k x 500k, d=64) and 4 (Doob, 500k, d=66) at full size: the
+    normalised operators on seeded row subsets against exact fp64 sums over all keys, with the
+    scales computed by the library (the scales themselves are checked at small sizes)."""
+    from flashdiffusion_b200 import synthetic
+    from flashdiffusion_b200.distributed import ShardedOperator
+    Q, K, beta = synthetic.amap_manifold(n=500_000, d=64, seed=0)
+    op = ShardedOperator(torch.from_numpy(Q).cuda(), torch.from_numpy(K).cuda(), beta, 0.5, "f16",
+                         mode="amap").fit()
+    v = np.random.default_rng(6).standard_normal(K.shape[0])
+    out = op.matvec_device(torch.from_numpy(v).cuda()).cpu().numpy()
+    rows = np.random.default_rng(7).choice(Q.shape[0], 12, replace=False)
+    rk, rq = op.rscale_k.double().cpu().numpy(), op.rscale_q.double().cpu().numpy()
+    ref = _exact_rows(Q[rows], K, rk * v, beta) * rq[rows]
+    assert rel_l2(out[rows], ref) <= TOL["f16"]
+
+    X, beta, h, _ = synthetic.langevin_trajectory(n_frames=500_000, d=66, seed=0)
+    op = ShardedOperator(torch.from_numpy(X).cuda(), None, beta, 0.5, "f16", mode="doob",
+                         h=torch.from_numpy(h).cuda()).fit()
+    out = op.matvec_device(torch.from_numpy(v).cuda()).cpu().numpy()
+    rs, ph = op.rscale_k.double().cpu().numpy(), op.ph.double().cpu().numpy()
+    ref = _exact_rows(X[rows], X, rs * h * v, beta) * rs[rows] / ph[rows]
+    assert rel_l2(out[rows], ref) <= TOL["f16"]
