@@ -308,18 +308,14 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
 // Sum the partials of row tiles cut between CTA ranges, in CTA order.
 __global__ void tc_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, RowEpilogue ep) {
     const int64_t rt = blockIdx.x;
-    int c_lo, c_hi;
-    cut_owners(sc, rt, &c_lo, &c_hi);
-    if (c_lo == c_hi) return;
     for (int r = threadIdx.x; r < ROWS; r += blockDim.x) {
         const int64_t gi = rt * ROWS + r;
         if (gi >= nq) continue;
         double sum = 0.0;
-        for (int c = c_lo; c <= c_hi; ++c) {
-            if (sc.start(c) == sc.start(c + 1)) continue;  // empty range
-            sum += part[((int64_t)c * 2 + cut_slot(sc, c, rt)) * ROWS + r];
-        }
-        store_out(ep, gi, 0, sum);
+        const bool cut = for_each_cut_owner(sc, rt, [&](int c, int slot) {
+            sum += part[((int64_t)c * 2 + slot) * ROWS + r];
+        });
+        if (cut) store_out(ep, gi, 0, sum);
     }
 }
 
@@ -589,18 +585,14 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
 // Fix-up of the wide kernel: 128-row tiles.
 __global__ void tcw_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, RowEpilogue ep) {
     const int64_t rt = blockIdx.x;
-    int c_lo, c_hi;
-    cut_owners(sc, rt, &c_lo, &c_hi);
-    if (c_lo == c_hi) return;
     for (int r = threadIdx.x; r < w::BM; r += blockDim.x) {
         const int64_t gi = rt * w::BM + r;
         if (gi >= nq) continue;
         double sum = 0.0;
-        for (int c = c_lo; c <= c_hi; ++c) {
-            if (sc.start(c) == sc.start(c + 1)) continue;
-            sum += part[((int64_t)c * 2 + cut_slot(sc, c, rt)) * w::BM + r];
-        }
-        store_out(ep, gi, 0, sum);
+        const bool cut = for_each_cut_owner(sc, rt, [&](int c, int slot) {
+            sum += part[((int64_t)c * 2 + slot) * w::BM + r];
+        });
+        if (cut) store_out(ep, gi, 0, sum);
     }
 }
 

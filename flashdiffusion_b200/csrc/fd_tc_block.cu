@@ -60,8 +60,7 @@ __device__ __forceinline__ bool timed_wait(int slot, uint64_t* b, uint32_t ph, v
 
 using tc::Sched;
 using tc::Walk;
-using tc::cut_owners;
-using tc::cut_slot;
+using tc::for_each_cut_owner;
 
 constexpr int BM = 128;
 constexpr int BN = 128;                    // keys per tile (N of Q.K^T, K of P.U)
@@ -514,19 +513,15 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
 __global__ void tc_block_fixup_kernel(const double* __restrict__ part, Sched sc, int64_t nq, int rc, int rp,
                                       RowEpilogue ep) {
     const int64_t rt = blockIdx.x;
-    int c_lo, c_hi;
-    cut_owners(sc, rt, &c_lo, &c_hi);
-    if (c_lo == c_hi) return;
     for (int e = threadIdx.x; e < BM * rc; e += blockDim.x) {
         const int r = e / rc, col = e % rc;
         const int64_t gi = rt * BM + r;
         if (gi >= nq) continue;
         double sum = 0.0;
-        for (int c = c_lo; c <= c_hi; ++c) {
-            if (sc.start(c) == sc.start(c + 1)) continue;
-            sum += part[(((int64_t)c * 2 + cut_slot(sc, c, rt)) * BM + r) * rp + col];
-        }
-        store_out(ep, gi, col, sum);
+        const bool cut = for_each_cut_owner(sc, rt, [&](int c, int slot) {
+            sum += part[(((int64_t)c * 2 + slot) * BM + r) * rp + col];
+        });
+        if (cut) store_out(ep, gi, col, sum);
     }
 }
 

@@ -24,85 +24,112 @@ struct Geo {
 };
 
 // Work split of the persistent kernels over (row tile, key tile) units.
-// First `full` whole row tiles per CTA, CTA c taking rows c, c + grid, ...:
-// every CTA starts each of these rows at key tile 0 at about the same time, so
-// the CTAs sweep K in near lockstep and a key tile is read from DRAM once per
-// sweep and then served from L2 (with CTAs at scattered key offsets, a K larger
-// than L2 is streamed from DRAM once per CTA).  The remaining row tiles
-// (fewer than grid) are cut into grid contiguous ranges of units; a row tile
-// cut between ranges leaves fp64 partials that the fix-up kernel sums in CTA
-// order (deterministic).
+//
+// Contiguous mode (the key operand stays in L2): the units, row-major, are cut
+// into grid contiguous ranges, one per CTA; a row tile cut between ranges
+// leaves fp64 partials that the fix-up kernel sums in CTA order.
+//
+// Lockstep mode (a key operand larger than L2): first `full` whole row tiles per
+// CTA, CTA c taking rows c, c + grid, ...: every CTA starts each of these rows at
+// key tile 0 at about the same time, so the CTAs sweep K in near lockstep and a
+// key tile is read from DRAM once per sweep and then served from L2 (with CTAs
+// at scattered key offsets, a K larger than L2 is streamed from DRAM once per
+// CTA).  The n_rem remaining row tiles (fewer than grid) are each cut into
+// k = grid / n_rem key chunks: CTA c < k n_rem takes row c mod n_rem, chunk
+// c / n_rem, so the CTAs of one chunk index again read the same key tiles
+// together; the chunks' partials are summed by the fix-up in chunk order.
+// Everything is deterministic.
 struct Sched {
     int64_t n_jt;    // key tiles per row tile
-    int64_t units;   // units of the remainder region: (n_rt - full * grid) * n_jt
-    int64_t full;    // whole row tiles per CTA
+    int64_t units;   // contiguous mode: units of the remainder region, (n_rt - full * grid) * n_jt
+    int64_t full;    // whole row tiles per CTA (lockstep mode)
+    int64_t n_rem;   // lockstep mode: remainder row tiles
+    int k;           // lockstep mode: key chunks per remainder row (0 = contiguous mode)
     int grid;
     __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }   // remainder range
     __host__ __device__ int64_t rem_rt0() const { return full * grid; }
+    __host__ __device__ int64_t chunk0(int j) const { return (int64_t)j * n_jt / k; }
     // schedule for n_rt row tiles of n_jt key tiles on at most `sms` CTAs; the
-    // lockstep rows only pay when the key operand does not stay in L2 anyway
+    // lockstep mode only pays when the key operand does not stay in L2 anyway
     // (measured: +17 % at 288 MB of keys, through lower DRAM power and higher
-    // clocks under the power cap; -3 % at 32 MB), so below `key_bytes` of
-    // 48 MB every unit goes to the contiguous ranges
+    // clocks under the power cap; -3 % at 32 MB), so it starts above 48 MB
     static Sched make(int64_t n_rt, int64_t n_jt, int sms, size_t key_bytes) {
         Sched sc;
         sc.n_jt = n_jt;
         const int64_t total = n_rt * n_jt;
         sc.grid = (int)(total < sms ? total : sms);
-        const bool lockstep = key_bytes > ((size_t)48 << 20);
-        sc.full = (lockstep && n_rt >= sc.grid) ? n_rt / sc.grid : 0;
-        sc.units = (n_rt - sc.full * sc.grid) * n_jt;
+        const bool lockstep = key_bytes > ((size_t)48 << 20) && n_jt >= sc.grid;
+        sc.full = lockstep ? n_rt / sc.grid : 0;
+        sc.n_rem = n_rt - sc.full * sc.grid;
+        sc.k = (lockstep && sc.n_rem > 0) ? (int)(sc.grid / sc.n_rem) : 0;
+        sc.units = sc.k ? 0 : sc.n_rem * n_jt;
         return sc;
     }
 };
 
-// One CTA's units in processing order (the same sequence in every role).
+// One CTA's units in processing order (the same sequence in every role).  The
+// schedule's own fields are read from the kernel parameter, not copied, to keep
+// the register count of the roles that carry a Walk down.
 struct Walk {
-    int64_t s = 0, steps, nfull, rt, jt, rem_first_rt, rem_u0;
-    int64_t n_jt, grid, rem_rt0;
-    __device__ Walk(const Sched& sc, int c) {
-        n_jt = sc.n_jt;
-        grid = sc.grid;
-        rem_rt0 = sc.rem_rt0();
-        nfull = sc.full * sc.n_jt;
-        rem_u0 = sc.start(c);
-        steps = nfull + sc.start(c + 1) - rem_u0;
-        rem_first_rt = rem_rt0 + rem_u0 / n_jt;
-        if (nfull > 0) {
+    const Sched& sc;
+    int64_t s = 0, steps, rt, jt, rem_first_rt, rem_jt0;
+    __device__ Walk(const Sched& sc_, int c) : sc(sc_) {
+        const int64_t rem_rt0 = sc.rem_rt0();
+        if (sc.k > 0) {
+            const bool busy = c < sc.k * sc.n_rem;
+            const int j = busy ? (int)(c / sc.n_rem) : 0;
+            rem_first_rt = rem_rt0 + (busy ? c % sc.n_rem : 0);
+            rem_jt0 = sc.chunk0(j);
+            steps = sc.full * sc.n_jt + (busy ? sc.chunk0(j + 1) - rem_jt0 : 0);
+        } else {
+            const int64_t u0 = sc.start(c);
+            rem_first_rt = rem_rt0 + u0 / sc.n_jt;
+            rem_jt0 = u0 - (rem_first_rt - rem_rt0) * sc.n_jt;
+            steps = sc.full * sc.n_jt + sc.start(c + 1) - u0;
+        }
+        if (sc.full > 0) {
             rt = c;
             jt = 0;
         } else {
             rt = rem_first_rt;
-            jt = rem_u0 - (rt - rem_rt0) * n_jt;
+            jt = rem_jt0;
         }
     }
     __device__ bool done() const { return s >= steps; }
     __device__ void next() {
         ++s;
+        const int64_t nfull = sc.full * sc.n_jt;
         if (s == nfull) {
             rt = rem_first_rt;
-            jt = rem_u0 - (rt - rem_rt0) * n_jt;
-        } else if (++jt == n_jt) {
+            jt = rem_jt0;
+        } else if (++jt == sc.n_jt) {
             jt = 0;
-            rt += s < nfull ? grid : 1;
+            rt += s < nfull ? sc.grid : 1;
         }
     }
     // last unit of this CTA's segment of row tile rt
-    __device__ bool seg_last() const { return jt + 1 == n_jt || s + 1 == steps; }
+    __device__ bool seg_last() const { return jt + 1 == sc.n_jt || s + 1 == steps; }
     // the segment covers all key tiles of the row (then the output is final)
     __device__ bool seg_full() const {
-        const bool starts_at_0 = s < nfull || rt != rem_first_rt || rem_u0 == (rt - rem_rt0) * n_jt;
-        return starts_at_0 && jt == n_jt - 1;
+        const bool starts_at_0 = s < sc.full * sc.n_jt || rt != rem_first_rt || rem_jt0 == 0;
+        return starts_at_0 && jt == sc.n_jt - 1;
     }
     // partial-sum slot of a cut row: 0 = the first remainder row, 1 = the last
     __device__ int slot() const { return rt == rem_first_rt ? 0 : 1; }
 };
 
-// Fix-up helper: the CTAs whose remainder ranges touch row tile rt
-// (c_lo == c_hi: the row was not cut; whole rows are never cut).
-__device__ inline void cut_owners(const Sched& sc, int64_t rt, int* c_lo, int* c_hi) {
-    *c_lo = *c_hi = 0;
-    if (rt < sc.rem_rt0()) return;
+// Fix-up helper: calls f(c, slot) for every CTA holding a partial of row tile
+// rt, in a fixed order; returns false (and calls nothing) when the row was not
+// cut (its owner wrote it directly).
+template <class F>
+__device__ inline bool for_each_cut_owner(const Sched& sc, int64_t rt, F f) {
+    if (rt < sc.rem_rt0()) return false;
+    if (sc.k > 0) {
+        if (sc.k == 1) return false;
+        const int64_t r = rt - sc.rem_rt0();
+        for (int j = 0; j < sc.k; ++j) f((int)(r + j * sc.n_rem), 0);
+        return true;
+    }
     const int64_t lo = (rt - sc.rem_rt0()) * sc.n_jt, hi = lo + sc.n_jt - 1;
     auto owner = [&](int64_t n) {
         int c = (int)(n * sc.grid / sc.units);
@@ -111,12 +138,13 @@ __device__ inline void cut_owners(const Sched& sc, int64_t rt, int* c_lo, int* c
         while (c > 0 && sc.start(c) > n) --c;
         return c;
     };
-    *c_lo = owner(lo);
-    *c_hi = owner(hi);
-}
-// slot of CTA c's partial for row tile rt (c in [c_lo, c_hi], non-empty range)
-__device__ inline int cut_slot(const Sched& sc, int c, int64_t rt) {
-    return (sc.rem_rt0() + sc.start(c) / sc.n_jt == rt) ? 0 : 1;
+    const int c_lo = owner(lo), c_hi = owner(hi);
+    if (c_lo == c_hi) return false;
+    for (int c = c_lo; c <= c_hi; ++c) {
+        if (sc.start(c) == sc.start(c + 1)) continue;   // empty range
+        f(c, (sc.rem_rt0() + sc.start(c) / sc.n_jt == rt) ? 0 : 1);
+    }
+    return true;
 }
 
 // ---- exp2 of a pair of exponents --------------------------------------------
