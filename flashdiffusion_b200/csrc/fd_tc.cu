@@ -328,16 +328,21 @@ __global__ void tc_fixup_kernel(const double* __restrict__ part, Sched sc, int64
 // streams each key tile as its 64-column boxes through a ring of 16 KB slots,
 // so the Q.K^T chain of a tile waits box by box; four TMEM S buffers (all 512
 // columns) let four epilogue warpgroups (tile m -> warpgroup m mod 4) overlap
-// the chain.  Warp roles (18 warps): 0-15 epilogue, 16 TMA producer (query
-// tile once per row tile, key boxes, u through a 4-deep ring), 17 the MMA
-// issuer.  The tensor pipe bounds it: 2 kd flops per evaluation.
+// the chain.  Two independent producer -> issuer pipelines, one for the even
+// and one for the odd tiles, each with its own half of the box ring (a single
+// consumer per sub-ring, in order), so the chain of one waits on a box while
+// the other's keeps the tensor pipe fed.  Warp roles (20 warps): 0-15 epilogue,
+// 16 / 19 TMA producers of the even / odd tiles (16 also loads the query tile
+// once per row tile; u through a 4-deep ring), 17 / 18 the MMA issuers of the
+// even / odd tiles.  2 kd tensor flops per evaluation.
 namespace w {
 constexpr int BM = 128;                 // query rows per tile = TMEM lanes
 constexpr int BN = 128;                 // keys per tile
 constexpr int NSB = 4;                  // S buffers = epilogue warpgroups
-constexpr int TMA_WARP = 16;
-constexpr int MMA_WARP = 17;
-constexpr int NTHREADS = 18 * 32;
+constexpr int TMA_WARP = 16;           // producer of the even tiles (and of the query tile)
+constexpr int MMA_WARP = 17;           // issuer of the even tiles; 18: odd tiles
+constexpr int TMA_WARP_ODD = 19;       // producer of the odd tiles
+constexpr int NTHREADS = 20 * 32;
 constexpr uint32_t SLOT_BYTES = BN * 128;   // one 64-column box of a key tile
 
 template <int KF, int NW>
@@ -347,12 +352,13 @@ struct Cfg {
     static constexpr uint32_t NARROW_BYTES = BN * NW * 2;
     static constexpr int SLOTS_RAW = (int)((221u * 1024u - Q_BYTES - URING * U_BYTES) / SLOT_BYTES);
     static constexpr int SLOTS = SLOTS_RAW > 12 ? 12 : SLOTS_RAW;
-    static_assert(SLOTS >= 3, "shared memory budget");
+    static_assert(SLOTS >= 4, "shared memory budget");
+    static constexpr int SH = SLOTS / 2;                               // slots per pipeline
     static constexpr uint32_t RING_OFF = (Q_BYTES + 1023) & ~1023u;
     static constexpr uint32_t U_OFF = RING_OFF + SLOTS * SLOT_BYTES;
     static constexpr uint32_t BAR_OFF = U_OFF + URING * U_BYTES;
-    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4], rfull, rempty, done
-    static constexpr int NBARS = 2 * SLOTS + 2 * URING + 2 + 2 * NSB + 3;
+    // kfull[S], kempty[S], ufull[U], uempty[U], qfull, qempty, sfull[4], sempty[4], rfull, rempty, done[2]
+    static constexpr int NBARS = 2 * SLOTS + 2 * URING + 2 + 2 * NSB + 4;
     static constexpr uint32_t MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr uint32_t RED_OFF = (MISC_OFF + 16 + 15) & ~15u;
     static constexpr uint32_t SMEM_BYTES = RED_OFF + (NSB - 1) * BM * 8;
@@ -403,14 +409,15 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
             ptx::mbar_init(&uempty[i], 4);      // the 4 warps of the warpgroup of tile m = i (mod 4)
         }
         ptx::mbar_init(qfull, 1);
-        ptx::mbar_init(qempty, 1);
+        ptx::mbar_init(qempty, 2);                  // both issuers, at every row-tile end
         for (int i = 0; i < w::NSB; ++i) {
             ptx::mbar_init(&sfull[i], 1);
             ptx::mbar_init(&sempty[i], 4);
         }
         ptx::mbar_init(rfull, (w::NSB - 1) * w::BM);   // every thread of warpgroups 1-3
         ptx::mbar_init(rempty, w::BM);                 // every thread of warpgroup 0
-        ptx::mbar_init(done, 1);
+        ptx::mbar_init(&done[0], 1);
+        ptx::mbar_init(&done[1], 1);
         *abort = 0;
         ptx::fence_mbar_init();
     }
@@ -427,14 +434,14 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == w::TMA_WARP) {
+    if (warp == w::TMA_WARP || warp == w::TMA_WARP_ODD) {
         if (lane == 0) {
-            int slot = 0;
-            uint32_t kph = 0, qcount = 0;
+            const int pp = warp == w::TMA_WARP ? 0 : 1;   // this producer's tile parity
+            uint32_t qcount = 0;
             int64_t cur_rt = -1;
             for (Walk wk(sc, cta); !wk.done(); wk.next()) {
                 const int64_t m = wk.s, rt = wk.rt, jt = wk.jt;
-                if (rt != cur_rt) {
+                if (pp == 0 && rt != cur_rt) {
                     if (qcount > 0 && !ptx::wait_bounded(qempty, (qcount - 1) & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ptx::mbar_expect_tx(qfull, C::Q_BYTES);
                     for (int kb = 0; kb < KF; ++kb)
@@ -443,8 +450,13 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
                     cur_rt = rt;
                     ++qcount;
                 }
+                if ((int)(m & 1) != pp) continue;
                 bool ok = true;
                 for (int kb = 0; kb < C::NB; ++kb) {
+                    // position in this pipeline's sub-ring, consumed in order by one issuer
+                    const int64_t pos = (m >> 1) * C::NB + kb;
+                    const int slot = pp * C::SH + (int)(pos % C::SH);
+                    const uint32_t kph = (uint32_t)((pos / C::SH) & 1);
                     if (!ptx::wait_bounded(&kempty[slot], kph ^ 1, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
                     uint8_t* dst = sR + slot * w::SLOT_BYTES;
                     if (kb < KF) {
@@ -454,7 +466,6 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
                         ptx::mbar_expect_tx(&kfull[slot], C::NARROW_BYTES);
                         ptx::tma_load_2d(dst, &tmk_n, &kfull[slot], KF * 64, (int)(jt * w::BN));
                     }
-                    if (++slot == C::SLOTS) { slot = 0; kph ^= 1; }
                 }
                 if (!ok) break;
                 const int us = (int)(m & (URING - 1));
@@ -464,11 +475,11 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
                 ptx::bulk_load(sU + us * w::BN, u + jt * w::BN, U_BYTES, &ufull[us]);
             }
         }
-    } else if (warp == w::MMA_WARP) {
+    } else if (warp == w::MMA_WARP || warp == w::MMA_WARP + 1) {
         if (lane == 0) {
+            const int pp = warp - w::MMA_WARP;             // this issuer's tile parity
             const uint32_t q_base = ptx::smem_u32(sQ), r_base = ptx::smem_u32(sR);
-            int slot = 0;
-            uint32_t kph = 0, qcount = 0;
+            uint32_t qcount = 0;
             int64_t cur_rt = -1;
             for (Walk wk(sc, cta); !wk.done(); wk.next()) {
                 const int64_t m = wk.s, rt = wk.rt;
@@ -478,36 +489,40 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
                     ++qcount;
                     cur_rt = rt;
                 }
-                if (!ptx::wait_bounded(&sempty[b], (uint32_t)(((m / w::NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
-                bool ok = true;
-                for (int kb = 0; kb < C::NB; ++kb) {
-                    if (!ptx::wait_bounded(&kfull[slot], kph, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
-                    ptx::tc_fence_after();
-                    const uint32_t ka = r_base + slot * w::SLOT_BYTES;
-                    if (kb < KF) {
-                        const uint32_t qa = q_base + kb * w::BM * 128;
+                if ((int)(m & 1) == pp) {
+                    if (!ptx::wait_bounded(&sempty[b], (uint32_t)(((m / w::NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
+                    bool ok = true;
+                    for (int kb = 0; kb < C::NB; ++kb) {
+                        const int64_t pos = (m >> 1) * C::NB + kb;
+                        const int slot = pp * C::SH + (int)(pos % C::SH);
+                        const uint32_t kph = (uint32_t)((pos / C::SH) & 1);
+                        if (!ptx::wait_bounded(&kfull[slot], kph, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t ka = r_base + slot * w::SLOT_BYTES;
+                        if (kb < KF) {
+                            const uint32_t qa = q_base + kb * w::BM * 128;
 #pragma unroll
-                        for (int ks = 0; ks < 4; ++ks)
-                            ptx::umma_ss(tmem + b * w::BN, ptx::sw128_kmajor_desc(qa + ks * 32),
-                                         ptx::sw128_kmajor_desc(ka + ks * 32), idesc, (kb | ks) ? 1u : 0u);
-                    } else {
-                        const uint32_t qa = q_base + KF * w::BM * 128;
+                            for (int ks = 0; ks < 4; ++ks)
+                                ptx::umma_ss(tmem + b * w::BN, ptx::sw128_kmajor_desc(qa + ks * 32),
+                                             ptx::sw128_kmajor_desc(ka + ks * 32), idesc, (kb | ks) ? 1u : 0u);
+                        } else {
+                            const uint32_t qa = q_base + KF * w::BM * 128;
 #pragma unroll
-                        for (int ks = 0; ks < NW / 16; ++ks) {
-                            const uint64_t dq = NW == 32 ? ptx::sw64_kmajor_desc(qa + ks * 32) : ptx::sw32_kmajor_desc(qa + ks * 32);
-                            const uint64_t dk = NW == 32 ? ptx::sw64_kmajor_desc(ka + ks * 32) : ptx::sw32_kmajor_desc(ka + ks * 32);
-                            ptx::umma_ss(tmem + b * w::BN, dq, dk, idesc, 1u);
+                            for (int ks = 0; ks < NW / 16; ++ks) {
+                                const uint64_t dq = NW == 32 ? ptx::sw64_kmajor_desc(qa + ks * 32) : ptx::sw32_kmajor_desc(qa + ks * 32);
+                                const uint64_t dk = NW == 32 ? ptx::sw64_kmajor_desc(ka + ks * 32) : ptx::sw32_kmajor_desc(ka + ks * 32);
+                                ptx::umma_ss(tmem + b * w::BN, dq, dk, idesc, 1u);
+                            }
                         }
+                        ptx::umma_commit(&kempty[slot]);
                     }
-                    ptx::umma_commit(&kempty[slot]);
-                    if (++slot == C::SLOTS) { slot = 0; kph ^= 1; }
+                    if (!ok) break;
+                    ptx::umma_commit(&sfull[b]);
                 }
-                if (!ok) break;
-                ptx::umma_commit(&sfull[b]);
                 if (wk.seg_last()) ptx::umma_commit(qempty);
             }
-            ptx::umma_commit(done);
-            ptx::wait_bounded(done, 0, abort, status, WAIT_LIMIT_NS);
+            ptx::umma_commit(&done[pp]);
+            ptx::wait_bounded(&done[pp], 0, abort, status, WAIT_LIMIT_NS);
         }
     } else if (warp < 16) {
         // ---- epilogue: warpgroup wg owns S buffer wg and the tiles m = wg (mod 4)
