@@ -73,7 +73,7 @@ struct Sched {
 struct Walk {
     const Sched& sc;
     int64_t s = 0, steps, rt, jt, rem_first_rt, rem_jt0;
-    __device__ Walk(const Sched& sc_, int c) : sc(sc_) {
+    __host__ __device__ Walk(const Sched& sc_, int c) : sc(sc_) {
         const int64_t rem_rt0 = sc.rem_rt0();
         if (sc.k > 0) {
             const bool busy = c < sc.k * sc.n_rem;
@@ -95,8 +95,8 @@ struct Walk {
             jt = rem_jt0;
         }
     }
-    __device__ bool done() const { return s >= steps; }
-    __device__ void next() {
+    __host__ __device__ bool done() const { return s >= steps; }
+    __host__ __device__ void next() {
         ++s;
         const int64_t nfull = sc.full * sc.n_jt;
         if (s == nfull) {
@@ -108,21 +108,21 @@ struct Walk {
         }
     }
     // last unit of this CTA's segment of row tile rt
-    __device__ bool seg_last() const { return jt + 1 == sc.n_jt || s + 1 == steps; }
+    __host__ __device__ bool seg_last() const { return jt + 1 == sc.n_jt || s + 1 == steps; }
     // the segment covers all key tiles of the row (then the output is final)
-    __device__ bool seg_full() const {
+    __host__ __device__ bool seg_full() const {
         const bool starts_at_0 = s < sc.full * sc.n_jt || rt != rem_first_rt || rem_jt0 == 0;
         return starts_at_0 && jt == sc.n_jt - 1;
     }
     // partial-sum slot of a cut row: 0 = the first remainder row, 1 = the last
-    __device__ int slot() const { return rt == rem_first_rt ? 0 : 1; }
+    __host__ __device__ int slot() const { return rt == rem_first_rt ? 0 : 1; }
 };
 
 // Fix-up helper: calls f(c, slot) for every CTA holding a partial of row tile
 // rt, in a fixed order; returns false (and calls nothing) when the row was not
 // cut (its owner wrote it directly).
 template <class F>
-__device__ inline bool for_each_cut_owner(const Sched& sc, int64_t rt, F f) {
+__host__ __device__ inline bool for_each_cut_owner(const Sched& sc, int64_t rt, F f) {
     if (rt < sc.rem_rt0()) return false;
     if (sc.k > 0) {
         if (sc.k == 1) return false;
