@@ -18,7 +18,7 @@ def test_schedule_covers_every_unit_once():
         pytest.skip("nvcc not available")
     with tempfile.TemporaryDirectory() as td:
         exe = os.path.join(td, "sched_check")
-        subprocess.run([nvcc, "-std=c++17", "-O1", "-o", exe, os.path.join(HERE, "sched_check.cu")],
+        subprocess.run([nvcc, "-std=c++17", "-O1", "--expt-relaxed-constexpr", "-o", exe, os.path.join(HERE, "sched_check.cu")],
                        check=True, capture_output=True)
         r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stdout + r.stderr
