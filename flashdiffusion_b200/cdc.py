@@ -69,3 +69,8 @@ def metric_tensor(dm, eigenvalues, eigenvectors, pairs: Optional[list] = None):
     G[:, b, a] = gam
     M = torch.einsum("ikm,ilm->kl", G, G)
     return G.cpu().numpy(), M.cpu().numpy()
+
+
+def _apply_Pplus(dm, f) -> np.ndarray:
+    """The reference's private name for P+ f (``FD/cdc.py:103-130``), host in and out."""
+    return apply_pplus(dm, f).cpu().numpy()

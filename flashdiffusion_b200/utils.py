@@ -16,7 +16,7 @@ import torch
 from . import native
 from .kernel import to_device
 
-__all__ = ["median_bandwidth", "knn_bandwidth", "knn_sqdist", "nystrom_extend"]
+__all__ = ["median_bandwidth", "knn_bandwidth", "knn_sqdist", "nystrom_extend", "to_f32", "to_f64"]
 
 
 def median_bandwidth(X, subsample: int = 2000) -> float:
@@ -64,3 +64,13 @@ def knn_bandwidth(X, k: int = 7) -> np.ndarray:
 def nystrom_extend(dm, X_new, t: int = 1) -> np.ndarray:
     """Out-of-sample coordinates of a fitted, transformed DiffusionMap (``FD/utils.py:59-123``)."""
     return dm.nystrom(X_new, t=t)
+
+
+def to_f32(X) -> np.ndarray:
+    """dtype helper of the reference (``FD/utils.py:130-131``)."""
+    return np.asarray(X, dtype=np.float32)
+
+
+def to_f64(X) -> np.ndarray:
+    """dtype helper of the reference (``FD/utils.py:133-134``)."""
+    return np.asarray(X, dtype=np.float64)
