@@ -77,6 +77,21 @@ def test_argument_errors_before_launch(lib):
     assert lib.fd_apply(fake, 4, fake, 4, 3, 0, fake, native.DTYPE_F16, 1, None, None, None, None, fake, 0, fake, 1 << 20, None) == native.FD_ERR_ARG
     # reference trio: null rscale
     assert lib.fd_matvec(fake, 0, 4, 3, fake, None, 1.0, 0, fake, fake, 1 << 20, None) == native.FD_ERR_ARG
+    # fp32-class split tiles: operand rows of at most 416 columns (d <= 136)
+    rc = lib.fd_pack_operand(fake, native.DTYPE_F32, 10, 137, None, 1.0, native.SIDE_QUERY, native.TILE_F16X3, fake, None)
+    assert rc == native.FD_ERR_ARG and b"416" in lib.fd_last_error()
+    # bandwidth selection: k out of range, more neighbours than keys, bad d
+    assert lib.fd_knn_sqdist(fake, 10, fake, 10, 3, 65, fake, None) == native.FD_ERR_ARG
+    assert lib.fd_knn_sqdist(fake, 10, fake, 4, 3, 5, fake, None) == native.FD_ERR_ARG
+    assert lib.fd_knn_sqdist(fake, 10, fake, 10, 0, 5, fake, None) == native.FD_ERR_ARG
+    assert lib.fd_pairwise_sqdist(fake, 70000, 3, fake, None) == native.FD_ERR_ARG
+    # RoPE windows: window sample index outside the window
+    assert lib.fd_rope_windows(fake, 2, 2, fake, 1, 1, 10, 2, 3, 1, 3, 1.0, None, 0, fake, fake, fake, None) == native.FD_ERR_ARG
+    # block options and the wait self-test validate their arguments
+    assert lib.fd_set_block_options(65, 0) == native.FD_ERR_ARG
+    assert lib.fd_set_block_options(0, 4) == native.FD_ERR_ARG
+    assert lib.fd_set_block_options(0, 0) == native.FD_OK
+    assert lib.fd_selftest_wait_timeout(10, None) == native.FD_ERR_ARG
 
 
 def test_no_device_raises_loudly():
