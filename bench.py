@@ -405,6 +405,12 @@ def run_ours(args):
     mufu_peak = 16 * 148 * sm_max * 1e6          # ex2 per s at max SM clock (measured 15.9/clk/SM)
     tensor_peak_evals = bf16_tf * 1e12 / flops_per_eval
     peak_evals = min(mufu_peak, tensor_peak_evals)
+    if lanczos is not None:
+        # the eigensolve against the same roofline: every product at the roofline rate
+        # (Lanczos: r = 1 products; LOBPCG: r-column block products, block_columns / r of them)
+        n_prod = lanczos.get("n_matvec") or sum(st["block_columns_applied"] for st in lanczos["stages"]) / r
+        lanczos["roofline_seconds"] = n_prod * evals / (peak_evals * world)
+        lanczos["roofline_frac"] = lanczos["roofline_seconds"] / lanczos["seconds"]
     cpu_baseline = None
     if world == 1:   # the host baseline is taken on rank 0 of a 1-GPU run only
         cs = CpuSampler(Q, K, beta, r)
