@@ -1,11 +1,15 @@
 """Benchmark of the FlashDiffusion DMAP matvec on B200 (kernel evals/s = N_q * N_k / t).
 
-Workload (default, ``--config c2``): configuration 2 of the benchmark set —
-N = 200,000 points in d = 64 from a seeded 10-component Gaussian mixture,
-median-rule beta, alpha = 0.5, one N(0,1) right-hand side; fp16 tensor-core
-tiles, fp32 accumulation.  A step is one normalised DMAP matvec
-out = rscale * K(rscale * v) over all N x N pairs (row-sharded over the GPUs
-for N > 1, followed by the NCCL all-gather of the output shards).
+Workload (default, ``--config c5``): configuration 5 of the benchmark set,
+the scale-out block DMAP — N = 2,000,000 points in d = 128 on a seeded
+10-dimensional tanh manifold, median-rule beta, alpha = 0.5, an N x 32 N(0,1)
+block right-hand side; fp16 tensor-core tiles, fp32 accumulation, P.V as a
+second tcgen05 GEMM.  A step is one normalised block DMAP product
+out = rscale * K(rscale * V) over all N x N pairs (row-sharded over the GPUs
+for N > 1, followed by the NCCL all-gather of the output shards).  After the
+timed steps: the r = 1 matvec on the same points (key ``c5r1``), and the time
+to k = 32 eigenpairs by LOBPCG on the block operator.  ``--config c2|c3|c4``
+measure the other configurations.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
        (N > 1: launched by torch.distributed.run, one rank per GPU)
@@ -32,16 +36,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIGS = {
-    "c2": dict(workload="c2: DMAP matvec, Gaussian mixture N=200000 d=64, r=1, alpha=0.5",
+    "c2": dict(workload="c2: DMAP matvec, Gaussian mixture N={n} d=64, r=1, alpha=0.5",
                n=200_000, d=64, r=1, mode="dmap"),
-    "c3": dict(workload="c3: AMAP matvec (Q != K), 6-D manifold N_q=N_k=500000 d=64, r=1, alpha=0.5",
+    "c3": dict(workload="c3: AMAP matvec (Q != K), 6-D manifold N_q=N_k={n} d=64, r=1, alpha=0.5",
                n=500_000, d=64, r=1, mode="amap"),
-    "c4": dict(workload="c4: Doob matvec, Langevin double well 500000 frames d=66, r=1, alpha=0.5",
+    "c4": dict(workload="c4: Doob matvec, Langevin double well {n} frames d=66, r=1, alpha=0.5",
                n=500_000, d=66, r=1, mode="doob"),
-    "c5": dict(workload="c5: DMAP block matvec, tanh manifold N=1000000 d=128, r=32, alpha=0.5",
-               n=1_000_000, d=128, r=32, mode="dmap"),
+    "c5": dict(workload="c5: DMAP block matvec, tanh manifold N={n} d=128, r=32, alpha=0.5",
+               n=2_000_000, d=128, r=32, mode="dmap"),
     # the north-star target: the single-vector DMAP matvec at the configuration-5 size
-    "c5r1": dict(workload="c5r1: DMAP matvec, tanh manifold N=1000000 d=128, r=1, alpha=0.5",
+    "c5r1": dict(workload="c5r1: DMAP matvec, tanh manifold N={n} d=128, r=1, alpha=0.5",
                  n=1_000_000, d=128, r=1, mode="dmap"),
 }
 
@@ -52,11 +56,11 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    p.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     p.add_argument("--no-lanczos", action="store_true")
     p.add_argument("--cpu-rows", type=int, default=0, help="rows of the CPU sample (0 = auto)")
     p.add_argument("--n", type=int, default=0, help="override the number of points (small profiling cases)")
-    p.add_argument("--lobpcg", action="store_true", help="block configurations: time LOBPCG to k = r eigenpairs")
+    p.add_argument("--no-lobpcg", action="store_true", help="block configurations: skip LOBPCG to k = r eigenpairs")
     p.add_argument("--lobpcg-tol", type=float, default=1e-3)
     p.add_argument("--lobpcg-tol2", type=float, default=1e-5)
     p.add_argument("--tiles", default="f16", choices=["f16", "bf16", "f16x3", "fp32"],
@@ -219,7 +223,23 @@ def load_peaks():
     return 6650.0, 1590.0, 1965.0, "fallback"
 
 
+def workload_config(name, beta):
+    """The `config` object of the JSON line: the workload only, identical in both arms."""
+    c = CONFIGS[name]
+    op_mb = c["n"] * (((c["d"] + 6 + 15) // 16) * 16) * 2 / 1e6
+    return {"workload": c["workload"].format(n=c["n"]), "n_q": c["n"], "n_k": c["n"], "d": c["d"], "r": c["r"],
+            "alpha": 0.5, "beta": beta, "mode": c["mode"], "seed": 0,
+            "l2": ("packed operand %.0f MB %s the 126 MB L2; the GPU arm writes 256 MB between timed steps"
+                   % (op_mb, "larger than" if op_mb > 126 else "within"))}
+
+
 def run_reference(args):
+    """The reference algorithm's CPU implementation, timed on the host cores.
+
+    Each step is a bounded sample of the workload (seeded query rows x all
+    keys, r right-hand-side columns), timed as a whole; `value` is the sampled
+    evaluations per second and `ms_per_step` the measured time of one sampled
+    step.  The projection to one full N x N product is a separate key."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -232,17 +252,20 @@ def run_reference(args):
     res = [cs.sample(rows, seed=s_) for s_ in range(args.steps)]
     cs.close()
     v = float(np.mean([x[0] for x in res]))
+    step_s = float(np.mean([x[1] for x in res]))
     cores = res[0][2]
     n = cfg["n"]
     line = {"impl": "reference", "metric": "kernel evals/sec per matvec (N^2/t)", "value": v, "unit": "evals/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * n * n / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "ms_per_step": 1e3 * step_s, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 GEMM + f64 exp/accumulate", "data": "synthetic (seeded generator)",
-            "config": {"workload": cfg["workload"], "n": n, "d": cfg["d"], "r": cfg["r"], "sample_rows": rows,
-                       "parallelism": "host processes, one BLAS thread each"},
+            "config": workload_config(args.config, beta),
+            "arm": {"kind": "host processes, one BLAS thread each", "sample_rows_per_step": rows,
+                    "evals_per_step": float(rows) * n},
+            "full_product_s_projected": float(n) * n / v,
             "cpu_baseline": {"value": v, "unit": "evals/s", "cores": cores, "kind": "port",
-                             "sample": f"{rows} seeded rows x all {n} keys per step over {cores} processes, "
-                                       "scaled to evals/s"},
+                             "sample": f"{rows} seeded rows x all {n} keys x r={cfg['r']} per step over {cores} "
+                                       "processes, scaled to evals/s"},
             "e2e": {"value": v, "unit": "evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
@@ -343,6 +366,28 @@ def run_ours(args):
     # Lanczos time to k eigenpairs through the precision ramp (16-bit tiles until
     # their rounding floor, then fp32-class tiles with an fp64 Rayleigh-Ritz),
     # device fp64 basis, outside the timed region
+    # block configurations: the single-vector (r = 1) DMAP matvec on the same
+    # points and operator, the north-star kernel (kernel-only events, L2 flushed)
+    r1 = None
+    if r > 1:
+        v1 = v[:, 0].contiguous()
+        for _ in range(2):
+            op.matvec_local(v1)
+        r1_ev = []
+        for _ in range(3):
+            flush.zero_()
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            op.matvec_local(v1)
+            b_.record()
+            r1_ev.append((a_, b_))
+        torch.cuda.synchronize()
+        t1 = torch.tensor([float(np.mean([x.elapsed_time(y) for x, y in r1_ev]))], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t1, op=dist.ReduceOp.MAX)
+        r1 = {"workload": f"DMAP matvec, r=1, same {nq} points and operator", "kernel_ms": float(t1.item()),
+              "value": float(nq) * nk / (float(t1.item()) / 1e3), "unit": "evals/s"}
+
     lanczos = None
     if not args.no_lanczos and cfg["mode"] in ("dmap", "doob") and r == 1:
         from flashdiffusion_b200.eigensolver import ramp_eigsh
@@ -368,7 +413,7 @@ def run_ours(args):
     # 8 key tiles per fp32 accumulation group to --lobpcg-tol, stage 2 warm-started
     # from stage 1 with one key tile per group (accumulation bias 8e-7) to
     # --lobpcg-tol2
-    if not args.no_lanczos and r > 1 and args.lobpcg:
+    if not args.no_lanczos and r > 1 and not args.no_lobpcg:
         from flashdiffusion_b200.eigensolver import SolveInfo, lobpcg_core
         stages, X, vals = [], None, None
         t00 = time.perf_counter()
@@ -411,6 +456,10 @@ def run_ours(args):
         n_prod = lanczos.get("n_matvec") or sum(st["block_columns_applied"] for st in lanczos["stages"]) / r
         lanczos["roofline_seconds"] = n_prod * evals / (peak_evals * world)
         lanczos["roofline_frac"] = lanczos["roofline_seconds"] / lanczos["seconds"]
+    if r1 is not None:
+        r1_peak = min(mufu_peak, bf16_tf * 1e12 / (2 * d))
+        r1["peak"] = r1_peak
+        r1["roofline_frac"] = r1["value"] / world / r1_peak
     cpu_baseline = None
     if world == 1:   # the host baseline is taken on rank 0 of a 1-GPU run only
         cs = CpuSampler(Q, K, beta, r)
@@ -435,9 +484,9 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": f"{args.tiles} tiles, f32 accumulate",
         "data": "synthetic (seeded generator)",
-        "config": {"workload": cfg["workload"], "n_q": nq, "n_k": nk, "d": d, "r": r, "beta": beta,
-                   "mode": cfg["mode"], "tiles": f"{op.op.precision} tcgen05" if op.op.precision != "fp32" else "fp32 SIMT", "parallelism": f"row-shard x{world}, NCCL all-gather",
-                   "l2": "flushed between steps (256 MB write)"},
+        "config": workload_config(args.config, beta),
+        "arm": {"tiles": f"{op.op.precision} tcgen05" if op.op.precision != "fp32" else "fp32 SIMT",
+                "parallelism": f"row-shard x{world}, NCCL all-gather of the output shards"},
         "roofline": {"bound": "mufu" if mufu_peak <= tensor_peak_evals else "tensor", "achieved": kern_evals,
                      "peak": peak_evals, "unit": "evals/s", "frac": kern_evals / peak_evals,
                      "traffic": TRAFFIC[args.config][0] if (args.config in TRAFFIC and not args.n and world == 1) else None,
@@ -453,7 +502,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": 8 * nq * r},
         "gpu_launches": (3 if r == 1 else 4) * args.steps,
         "prepass_s": prepass_s, "setup_s": setup_s, "kernel_ms": kern_ms,
-        "lanczos": lanczos, "clocks": clk,
+        "lanczos": lanczos, "c5r1": r1, "clocks": clk,
     }
     print(json.dumps(line))
     if world > 1:
