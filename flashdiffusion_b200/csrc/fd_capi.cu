@@ -36,10 +36,12 @@ static bool valid_tile(int t) {
     return t == FD_TILE_BF16 || t == FD_TILE_F32 || t == FD_TILE_F16 || t == FD_TILE_F16X3;
 }
 
-// columns of V handled per tile-kernel launch
+// columns of V handled per tile-kernel launch (an upper bound over d: operands
+// wider than the block kernel's limit take one column per launch, which needs
+// less)
 static int cols_per_launch(int tile, int r) {
     if (tile == FD_TILE_F32) return 64;
-    return r == 1 ? 1 : 64;
+    return r == 1 ? 1 : block_max_cols(0);
 }
 
 // prepared right-hand side: fp32 u (r = 1 tensor-core and fp32 paths) or the
@@ -142,7 +144,7 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
                  "workspace must be non-null and 256-byte aligned");
     if (nq == 0) return FD_OK;
 
-    // (the workspace query is sized for 64 block columns, an upper bound for any d)
+    // (the workspace query is sized for block_max_cols columns, an upper bound for any d)
     // block tensor-core path for r > 1 up to 208 operand columns; wider operands
     // (the 128-row streaming kernel) take one column per launch
     const bool wide = is_tc_tile(tile) && kd_tile(tile, d) > 208;

@@ -60,11 +60,16 @@ extern "C" int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, in
     FD_CHECK_ARG(nq >= 0 && nk >= 0 && r >= 1, "fd_apply_noalloc: bad shape nq=%lld nk=%lld r=%d",
                  (long long)nq, (long long)nk, r);
     const size_t need = fd_apply_workspace_bytes(nq, nk, r, tile);
-    if (need > (size_t)FD_NOALLOC_SCRATCH_BYTES)
+    if (need > (size_t)FD_NOALLOC_SCRATCH_BYTES) {
+        // the kernel's cross-CTA partial sums grow with r but not with nk; the
+        // rest of the scratch is the prepared right-hand side, linear in nk
+        const size_t fixed = fd_apply_workspace_bytes(nq, 0, r, tile);
         return set_error(FD_ERR_WORKSPACE,
-                         "fd_apply_noalloc: nk=%lld needs %zu B of scratch but the static scratch holds %zu B "
-                         "(about 1.9 million keys on a 148-SM GPU); use fd_apply with a workspace",
-                         (long long)nk, need, (size_t)FD_NOALLOC_SCRATCH_BYTES);
+                         "fd_apply_noalloc: nk=%lld, r=%d needs %zu B of scratch (%zu B of it even for one key) but "
+                         "the static scratch holds %zu B; limits on a 148-SM GPU: r=1 up to about 1.9 million keys, "
+                         "r=2..16 up to about 55,000 keys, r>=17 not supported; use fd_apply with a workspace",
+                         (long long)nk, r, need, fixed, (size_t)FD_NOALLOC_SCRATCH_BYTES);
+    }
     void* scratch = nullptr;
     FD_TRY(noalloc_scratch(&scratch));
     // Nothing in the scratch has to start at zero: the right-hand side region

@@ -24,6 +24,8 @@
 // workspace that tc_fixup_kernel sums in CTA order (deterministic).
 #include <cstdlib>
 
+#include <mutex>
+
 #include "fd_tc_common.cuh"
 
 namespace fd {
@@ -828,10 +830,16 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
 
 int status_word(int** ptr) {
     static int* cached[64] = {nullptr};
+    static std::mutex mu;
     int dev = 0;
     FD_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(FD_ERR_ARG, "device index %d out of range", dev);
-    if (!cached[dev]) FD_CUDA_TRY(cudaGetSymbolAddress((void**)&cached[dev], g_fd_status));
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cached[dev]) {
+        int* p = nullptr;
+        FD_CUDA_TRY(cudaGetSymbolAddress((void**)&p, g_fd_status));
+        cached[dev] = p;
+    }
     *ptr = cached[dev];
     return FD_OK;
 }

@@ -157,9 +157,13 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
  * inside the library, held on every GPU that loads the library until the
  * process exits.  Inputs, operands and the output are still the caller's.
  *
- * Limits: 16-bit tiles only (FD_TILE_F16 / FD_TILE_BF16); nk such that
- * fd_apply_workspace_bytes(nq, nk, r, tile) <= FD_NOALLOC_SCRATCH_BYTES (about
- * 1.9 million keys on a 148-SM B200), otherwise FD_ERR_WORKSPACE with a message.
+ * Limits: 16-bit tiles only (FD_TILE_F16 / FD_TILE_BF16) and
+ * fd_apply_workspace_bytes(nq, nk, r, tile) <= FD_NOALLOC_SCRATCH_BYTES, which
+ * on a 148-SM B200 means: r = 1 up to about 1.9 million keys; r = 2..16 up to
+ * about 55,000 keys (the block path's cross-CTA partial sums take 4.6 MiB
+ * whatever nk is); r >= 17 not supported (those partial sums alone exceed the
+ * array).  Larger sizes return FD_ERR_WORKSPACE with a message naming nk, r
+ * and the bytes needed, before any launch.
  * The first call on a device looks the array's device address up
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * All calls share the one array, so calls that overlap on the GPU (other
