@@ -22,7 +22,6 @@
 // ranges (persistent CTAs, one per SM).  A row tile fully inside one range is
 // written directly; a row tile cut between ranges leaves fp64 partials in the
 // workspace that tc_fixup_kernel sums in CTA order (deterministic).
-#include <cstdlib>
 
 #include <mutex>
 
@@ -699,14 +698,12 @@ static int launch_tc_kb(const TcArgs& a, cudaStream_t s) {
 // Columns per 16 whose exp2 runs on the FMA pipe instead of MUFU (degree-4
 // polynomial, relative error 3.6e-6): 4 by default for the 16-bit tiles, where
 // MUFU is the limit; 0 for the fp32-class tiles (their error budget is 1e-5).
-// FD_EXP2_FMA_COLS (0, 2, 4, 6 or 8) overrides it.
+// fd_set_exp2_fma_cols overrides the 16-bit default (0, 2, 4, 6 or 8).
+static int g_exp2_fma_cols = -1;
+
 static int exp2_fma_cols(int tile) {
-    const char* e = getenv("FD_EXP2_FMA_COLS");
-    if (e) {
-        const int x = atoi(e);
-        return (x == 2 || x == 4 || x == 6 || x == 8) ? x : 0;
-    }
-    return tile == FD_TILE_F16X3 ? 0 : 4;
+    if (tile == FD_TILE_F16X3) return 0;
+    return g_exp2_fma_cols >= 0 ? g_exp2_fma_cols : 4;
 }
 
 template <int KF, int NW>
@@ -877,6 +874,36 @@ extern "C" int fd_selftest_wait_timeout(int64_t limit_ns, void* stream) {
     int* status = nullptr;
     FD_TRY(fd::status_word(&status));
     wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(status, (uint64_t)limit_ns);
+    FD_CUDA_TRY(cudaGetLastError());
+    return FD_OK;
+}
+
+extern "C" int fd_set_exp2_fma_cols(int cols) {
+    FD_CHECK_ARG(cols == -1 || cols == 0 || cols == 2 || cols == 4 || cols == 6 || cols == 8,
+                 "fd_set_exp2_fma_cols: %d (-1 = default, or 0, 2, 4, 6, 8)", cols);
+    fd::g_exp2_fma_cols = cols;
+    return FD_OK;
+}
+
+namespace {
+__global__ void exp2_poly_selftest_kernel(const float* __restrict__ x, int64_t n, float* __restrict__ y) {
+    for (int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i < n;
+         i += 2 * (int64_t)gridDim.x * blockDim.x) {
+        const float a = x[i], b = i + 1 < n ? x[i + 1] : 0.0f;
+        uint32_t lo, hi;
+        fd::ptx::unpack2(fd::tc::exp2_poly2(__float_as_uint(a), __float_as_uint(b)), lo, hi);
+        y[i] = __uint_as_float(lo);
+        if (i + 1 < n) y[i + 1] = __uint_as_float(hi);
+    }
+}
+}  // namespace
+
+extern "C" int fd_selftest_exp2_poly(const float* x, int64_t n, float* y, void* stream) {
+    FD_CHECK_ARG(n >= 0 && (n == 0 || (x && y)), "fd_selftest_exp2_poly: bad arguments");
+    if (n == 0) return FD_OK;
+    const int64_t pairs = (n + 1) / 2;
+    const int grid = (int)((pairs + 255) / 256 < 148 * 8 ? (pairs + 255) / 256 : 148 * 8);
+    exp2_poly_selftest_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, n, y);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }

@@ -157,7 +157,7 @@ __device__ __forceinline__ uint64_t exp2_mufu2(uint32_t a, uint32_t b) {
 
 // FMA pipe: 2^x = 2^j 2^f, j = round(x) by the 1.5*2^23 shift, f = x - j in
 // [-1/2, 1/2], 2^f by a degree-4 polynomial (relative error 3.6e-6; fitted by
-// flashdiffusion_b200/csrc/exp2_poly_fit.py), 2^j added into the exponent
+// the Remez exchange in tests/test_exp2_poly.py), 2^j added into the exponent
 // field with one integer multiply-add.  x is clamped at -125 first so the
 // exponent field cannot underflow.
 __device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {

@@ -47,6 +47,8 @@ SIGNATURES = {
     "fd_dmap_rscale": (_I, [_P, _P, _L, _P, _P, _P]),
     "fd_set_block_options": (_I, [_I, _I]),
     "fd_selftest_wait_timeout": (_I, [_L, _P]),
+    "fd_set_exp2_fma_cols": (_I, [_I]),
+    "fd_selftest_exp2_poly": (_I, [_P, _L, _P, _P]),
     "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
     "fd_pairwise_sqdist": (_I, [_P, _L, _I, _P, _P]),
     "fd_rope_windows": (_I, [_P, _L, _L, _P, _L, _L, _L, _I, _I, _I, _I, ctypes.c_double, _P, _I, _P, _P, _P,
@@ -197,6 +199,19 @@ def dmap_rscale(Kw: torch.Tensor, w: torch.Tensor):
 def set_block_options(group_tiles: int = 0, products: int = 0) -> None:
     """Block-path options for later launches (0 = default); see include/fd_sm100.h."""
     check(load().fd_set_block_options(int(group_tiles), int(products)))
+
+
+def set_exp2_fma_cols(cols: int = -1) -> None:
+    """Columns per 16 of the 16-bit r = 1 epilogue on the FMA-pipe exp2 (-1 = default)."""
+    check(load().fd_set_exp2_fma_cols(int(cols)))
+
+
+def exp2_poly(x: torch.Tensor) -> torch.Tensor:
+    """The epilogues' FMA-pipe 2^x on a float32 device tensor (self-test entry point)."""
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    check(load().fd_selftest_exp2_poly(_ptr(x), x.numel(), _ptr(y), _stream(x.device)))
+    return y
 
 
 def check_status(device=None) -> None:

@@ -228,6 +228,18 @@ int fd_selftest_wait_timeout(int64_t limit_ns, void* stream);
  * launches from other host threads. */
 int fd_set_block_options(int group_tiles, int products);
 
+/* Share of the exponentials of the 16-bit r = 1 tile kernels that runs on the
+ * FMA pipe as a degree-4 polynomial (relative error below 3.7e-6) instead of
+ * MUFU ex2, in columns per 16: 0, 2, 4, 6 or 8; -1 restores the default (4;
+ * the fp32-class tiles always use MUFU).  Process-wide, for the next launches
+ * (no counterpart in the reference, whose kernel calls expf). */
+int fd_set_exp2_fma_cols(int cols);
+
+/* Self-test of the FMA-pipe exponential (no counterpart in the reference):
+ * y[i] = 2^x[i] computed exactly as the tile epilogues compute their
+ * polynomial share (x clamped at -125), fp32 device arrays of length n. */
+int fd_selftest_exp2_poly(const float* x, int64_t n, float* y, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Coifman-Lafon normalisation helpers (FD/dmap.py:108-115,
  * FD/kernel_cuda_sm100.py:89-98), fp32 vectors of length n.
