@@ -71,6 +71,40 @@ def _orth_against(Vb: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return h + h2
 
 
+def _native_rows_limit():
+    try:
+        from . import native
+        native.load()
+        return native.LANCZOS_MAX_ROWS
+    except (ImportError, OSError):
+        return 0
+
+
+def _lanczos_cycle(op, V, T, kk, m, N, it, device, info):
+    """Steps kk..m-1 of one restart cycle with host reads of the coefficients
+    (bases wider than the library's row limit, and breakdowns).  Returns the
+    last beta."""
+    beta = 0.0
+    for j in range(kk, m):
+        w = op(V[j]).to(torch.float64).reshape(-1).clone()
+        info.n_matvec += 1
+        h = _orth_against(V[: j + 1], w)
+        hc = h.cpu().numpy()
+        T[: j + 1, j] = hc
+        T[j, : j + 1] = hc
+        beta = float(torch.linalg.vector_norm(w))
+        if beta < 1e-300 or not np.isfinite(beta):
+            # invariant subspace: continue from a fresh orthogonal direction
+            g = torch.Generator(device="cpu").manual_seed(1000 + j + it)
+            w = torch.randn(N, generator=g, dtype=torch.float64).to(device)
+            _orth_against(V[: j + 1], w)
+            V[j + 1] = w / torch.linalg.vector_norm(w)
+            beta = 0.0
+        else:
+            V[j + 1] = w / beta
+    return beta
+
+
 def trlan(op: Callable[[torch.Tensor], torch.Tensor], N: int, k: int, tol: float, maxiter: int, ncv: int,
           v0: Optional[torch.Tensor], device, info: SolveInfo, stall_restarts: int = 3):
     """Thick-restart Lanczos for the k eigenvalues of largest magnitude.
@@ -92,25 +126,33 @@ def trlan(op: Callable[[torch.Tensor], torch.Tensor], N: int, k: int, tol: float
     best = np.inf
     stall = 0
     theta = Y = res = None
+    # the library's reorthogonalisation (three passes over V per step; the
+    # projected-matrix coefficients stay on the device and are read once per
+    # restart) whenever the basis fits its row limit
+    fast = device.type == "cuda" and m + 1 <= _native_rows_limit()
+    if fast:
+        from . import native
+        Tdev = torch.zeros((m, m + 2), dtype=torch.float64, device=device)
+        ws = native.lanczos_workspace(N, m + 1, device)
     for it in range(maxiter):
-        beta = 0.0
-        for j in range(kk, m):
-            w = op(V[j]).to(torch.float64).reshape(-1).clone()
-            info.n_matvec += 1
-            h = _orth_against(V[: j + 1], w)
-            hc = h.cpu().numpy()
-            T[: j + 1, j] = hc
-            T[j, : j + 1] = hc
-            beta = float(torch.linalg.vector_norm(w))
-            if beta < 1e-300 or not np.isfinite(beta):
-                # invariant subspace: continue from a fresh orthogonal direction
-                g = torch.Generator(device="cpu").manual_seed(1000 + j + it)
-                w = torch.randn(N, generator=g, dtype=torch.float64).to(device)
-                _orth_against(V[: j + 1], w)
-                V[j + 1] = w / torch.linalg.vector_norm(w)
-                beta = 0.0
+        if fast:
+            for j in range(kk, m):
+                w = op(V[j]).to(torch.float64).reshape(-1).contiguous()
+                info.n_matvec += 1
+                native.lanczos_reorth(V, j + 1, w, V[j + 1], Tdev[j], ws)
+            Tc = Tdev.cpu().numpy()
+            betas = np.array([Tc[j, j + 1] for j in range(kk, m)])
+            if np.all(np.isfinite(Tc[kk:m])) and np.all(betas > 1e-300):
+                for j in range(kk, m):
+                    T[: j + 1, j] = Tc[j, : j + 1]
+                    T[j, : j + 1] = Tc[j, : j + 1]
+                beta = float(betas[-1])
             else:
-                V[j + 1] = w / beta
+                # a breakdown (invariant subspace) in this cycle: redo it on the
+                # host-synchronised path, which continues from a fresh direction
+                beta = _lanczos_cycle(op, V, T, kk, m, N, it, device, info)
+        else:
+            beta = _lanczos_cycle(op, V, T, kk, m, N, it, device, info)
         Ts = 0.5 * (T + T.T)
         evals, evecs = np.linalg.eigh(Ts)
         order = np.argsort(-np.abs(evals))

@@ -48,6 +48,8 @@ SIGNATURES = {
     "fd_set_block_options": (_I, [_I, _I]),
     "fd_selftest_wait_timeout": (_I, [_L, _P]),
     "fd_set_exp2_fma_cols": (_I, [_I]),
+    "fd_lanczos_workspace_bytes": (_S, [_L, _I]),
+    "fd_lanczos_reorth": (_I, [_P, _L, _I, _L, _P, _P, _P, _P, _S, _P]),
     "fd_selftest_exp2_poly": (_I, [_P, _L, _P, _P]),
     "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
     "fd_pairwise_sqdist": (_I, [_P, _L, _I, _P, _P]),
@@ -212,6 +214,30 @@ def exp2_poly(x: torch.Tensor) -> torch.Tensor:
     y = torch.empty_like(x)
     check(load().fd_selftest_exp2_poly(_ptr(x), x.numel(), _ptr(y), _stream(x.device)))
     return y
+
+
+LANCZOS_MAX_ROWS = 96
+
+
+def lanczos_workspace(n: int, rows: int, device) -> torch.Tensor:
+    """Workspace for ``lanczos_reorth`` with up to ``rows`` basis rows."""
+    nb = int(load().fd_lanczos_workspace_bytes(int(n), int(rows)))
+    return torch.empty(nb + 256, dtype=torch.uint8, device=device)
+
+
+def lanczos_reorth(V: torch.Tensor, rows: int, w: torch.Tensor, out: torch.Tensor, coef: torch.Tensor,
+                   ws: torch.Tensor) -> None:
+    """CGS2 of w (overwritten) against V[:rows]: coef[:rows] = projections,
+    coef[rows] = beta, out = w2 / beta.  fp64 device tensors; no host sync."""
+    for t in (V, w, out, coef):
+        if t.dtype != torch.float64 or not t.is_cuda:
+            raise TypeError("lanczos_reorth: fp64 CUDA tensors expected")
+    if V.stride(1) != 1 or not (w.is_contiguous() and out.is_contiguous() and coef.is_contiguous()):
+        raise ValueError("lanczos_reorth: contiguous rows expected")
+    base = ws.data_ptr()
+    aligned = (base + 255) & ~255
+    check(load().fd_lanczos_reorth(_ptr(V), V.stride(0), int(rows), V.shape[1], _ptr(w), _ptr(out), _ptr(coef),
+                                   ctypes.c_void_p(aligned), ws.numel() - (aligned - base), _stream(V.device)))
 
 
 def check_status(device=None) -> None:

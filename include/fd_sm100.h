@@ -176,6 +176,26 @@ int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, int64_t nk, i
                      void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Lanczos vector operations (fp64, device).  Replace the host-side fp64
+ * reorthogonalisation inside ARPACK that lanczos_eigsh (FD/eigensolver.py:33-85)
+ * relies on; FD/eigensolver.py:17-20 states the fp64 basis requirement.
+ * ------------------------------------------------------------------------- */
+
+/* Workspace for fd_lanczos_reorth with n entries and `rows` basis rows. */
+size_t fd_lanczos_workspace_bytes(int64_t n, int rows);
+
+/* One Lanczos step's full reorthogonalisation.  V is a row-major fp64 basis
+ * (row i at V + i*ldv, n entries, rows orthonormal), w the operator output
+ * (overwritten).  Classical Gram-Schmidt applied twice against rows [0, rows):
+ * coef[0..rows) = V w + V w1 (the projected-matrix column), coef[rows] = beta
+ * = ||w2||, out (n entries; may be row `rows` of V) = w2 / beta, or zeros if
+ * beta <= 1e-300 (the caller then restarts from a fresh vector).  Three passes
+ * over V, fixed-order reductions (bit-reproducible), no host synchronisation.
+ * 1 <= rows <= 96. */
+int fd_lanczos_reorth(const double* V, int64_t ldv, int rows, int64_t n, double* w, double* out,
+                      double* coef, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Bandwidth selection (FD/utils.py:16-52), fp32 row-major inputs, fp32 CUDA-core
  * arithmetic on coordinate differences.
  * ------------------------------------------------------------------------- */
