@@ -28,6 +28,8 @@ from __future__ import annotations
 
 from typing import Optional
 
+import warnings
+
 import numpy as np
 import torch
 
@@ -134,6 +136,12 @@ class GaussianOperator:
                 if self.tile == native.TILE_F16X3:
                     self.tile, self.precision = native.TILE_F32, "fp32"
                 else:
+                    # bf16 operands round 8x more coarsely: their matvec error
+                    # budget is 1e-2, not the 2e-3 of the fp16 tiles
+                    warnings.warn("flashdiffusion_b200: packed fp16 tile values would overflow for these points "
+                                  "and beta; falling back to bf16 tiles, whose matvec relative error bound is "
+                                  "1e-2 instead of 2e-3 (pass precision='f16x3' or 'fp32' for tighter results)",
+                                  RuntimeWarning, stacklevel=2)
                     self.tile, self.precision = native.TILE_BF16, "bf16"
         if self.tile not in (native.TILE_F16, native.TILE_F16X3):
             self.qop = native.pack(Qd, self.beta, native.SIDE_QUERY, self.tile, self.shift)

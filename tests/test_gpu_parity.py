@@ -419,6 +419,42 @@ def test_c5_full_size_properties():
     assert rel_l2(out[rows], ref) <= TOL["f16"]
 
 
+def test_c5_full_size_block_product():
+    """Configuration 5's block product at 1M points (d=128, r=32, one tcgen05 block-kernel pass
+    with the DMAP scales): every column on a seeded row subset against exact fp64 sums over all
+    1M keys, and the exact eigenvector sqrt(D_alpha) carried in one column of the block (its
+    tolerance is the block path's fp32 accumulation bias, about 6e-6 with the default 8 key
+    tiles per tensor-core accumulation group)."""
+    from flashdiffusion_b200 import GaussianOperator, synthetic
+    from flashdiffusion_b200.kernel_cuda_sm100 import normalise
+    X, beta = synthetic.tanh_manifold(n=1_000_000, d=128, seed=0)
+    n = X.shape[0]
+    op = GaussianOperator(X, None, beta, "f16")
+    _, Da, rs = normalise(op, 0.5)
+    rng = np.random.default_rng(21)
+    V = rng.standard_normal((n, 32))
+    V[:, 1] = np.sin(3.0 * X[:, 0]) + 0.1          # a smooth column with cancellation
+    V[:, 2] *= 1e-3                                 # columns of very different scales
+    V[:, 3] *= 1e3
+    Vd = torch.from_numpy(V).cuda()
+    x = torch.sqrt(Da.double())
+    Vd[:, 0] = x
+    out = op.apply(Vd, col_scale=rs, row_scale=rs, out_dtype=torch.float64)
+    assert float(torch.linalg.vector_norm(out[:, 0] - x) / torch.linalg.vector_norm(x)) <= 1e-5
+    rows = np.random.default_rng(22).choice(n, 8, replace=False)
+    rsd = rs.double().cpu().numpy()
+    U = Vd.cpu().numpy() * rsd[:, None]
+    ref = np.zeros((len(rows), 32))
+    for c0 in range(0, n, 250_000):
+        Kc = X[c0:c0 + 250_000].astype(np.float64)
+        for i, r in enumerate(rows):
+            ref[i] += np.exp(-beta * ((Kc - X[r].astype(np.float64)) ** 2).sum(1)) @ U[c0:c0 + 250_000]
+    ref *= rsd[rows][:, None]
+    got = out.cpu().numpy()[rows]
+    for c in range(32):
+        assert rel_l2(got[:, c], ref[:, c]) <= TOL["f16"], c
+
+
 def _exact_rows(Qrows, K, u, beta, chunk=250_000):
     """Exact fp64 sum_j exp(-beta |q_i - k_j|^2) u_j for a few rows, keys in chunks."""
     ref = np.zeros(len(Qrows))
@@ -452,3 +488,18 @@ def test_c3_c4_full_size_row_subsets():
     rs, ph = op.rscale_k.double().cpu().numpy(), op.ph.double().cpu().numpy()
     ref = _exact_rows(X[rows], X, rs * h * v, beta) * rs[rows] / ph[rows]
     assert rel_l2(out[rows], ref) <= TOL["f16"]
+
+
+def test_fp16_overflow_falls_back_to_bf16_with_a_warning():
+    """Points whose packed fp16 values would overflow (two tight clusters far from their common
+    mean): the operator repacks in bf16 and says so, since bf16 tiles have the looser bound."""
+    from flashdiffusion_b200 import GaussianOperator
+    rng = np.random.default_rng(31)
+    X = rng.standard_normal((512, 8)).astype(np.float32)
+    X[:256] += 100.0
+    X[256:] -= 100.0
+    with pytest.warns(RuntimeWarning, match="bf16"):
+        op = GaussianOperator(X, None, 0.5, "f16")
+    assert op.precision == "bf16"
+    out = op.apply(torch.ones(512, dtype=torch.float64, device="cuda"), out_dtype=torch.float64)
+    assert bool(torch.isfinite(out).all())
