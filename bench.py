@@ -329,9 +329,9 @@ def run_ours(args):
     for i in range(args.steps):
         flush.zero_()                      # L2 flush between timed steps (outside the step events)
         starts[i].record()
-        vl = op.matvec_local(v)
+        vl = op.matvec_shard(v)
         ken[i].record()
-        op.gather(vl)
+        op.gather_shards(vl, r == 1)
         ends[i].record()
     torch.cuda.synchronize()
     if world > 1:

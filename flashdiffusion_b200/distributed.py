@@ -34,9 +34,12 @@ def all_shards(n: int, world: int, tile: int = ROW_TILE):
 class RowGather:
     """All-gather of uneven contiguous row shards into the full (n, r) array.
 
-    NCCL gathers equal-sized buffers, so shards are padded to the largest
-    shard and the valid rows are copied out afterwards (a device copy of n*r
-    elements).
+    NCCL gathers equal-sized chunks, so each rank's chunk is its shard padded
+    to the largest shard.  The padded buffer is allocated once per (r, dtype)
+    and reused; the tile kernel writes this rank's rows straight into its chunk
+    (``slot``), the all-gather runs in place, and the result is a view of the
+    buffer when every shard has the same size, else one gather-copy of the
+    valid rows.
     """
 
     def __init__(self, n: int, world: int, group=None):
@@ -45,17 +48,43 @@ class RowGather:
         self.group = group
         self.shards = all_shards(n, world)
         self.maxrows = max(b - a for a, b in self.shards)
+        self.rank = dist.get_rank(group) if (world > 1 and dist.is_initialized()) else 0
+        self.equal = all(b - a == self.maxrows for a, b in self.shards)
+        self._bufs = {}
+        self._index = None
+
+    def _buf(self, r: int, dtype, device) -> torch.Tensor:
+        key = (r, dtype, str(device))
+        if key not in self._bufs:
+            self._bufs[key] = torch.empty((self.world * self.maxrows, r), dtype=dtype, device=device)
+        return self._bufs[key]
+
+    def slot(self, r: int, dtype, device) -> torch.Tensor:
+        """This rank's (rows, r) chunk of the gather buffer, for the kernel to write into."""
+        a, b = self.shards[self.rank]
+        off = self.rank * self.maxrows
+        return self._buf(r, dtype, device)[off: off + (b - a)]
+
+    def gather_slot(self, r: int, dtype, device) -> torch.Tensor:
+        """All-gather the chunks written through ``slot``; returns the full (n, r) rows."""
+        buf = self._buf(r, dtype, device)
+        off = self.rank * self.maxrows
+        dist.all_gather_into_tensor(buf, buf[off: off + self.maxrows], group=self.group)
+        if self.equal:
+            return buf[: self.n]
+        if self._index is None or self._index.device != buf.device:
+            self._index = torch.cat([torch.arange(i * self.maxrows, i * self.maxrows + (b - a), device=buf.device)
+                                     for i, (a, b) in enumerate(self.shards)])
+        return buf.index_select(0, self._index)
 
     def __call__(self, local: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return local
         r = 1 if local.dim() == 1 else local.shape[1]
-        loc2 = local.reshape(local.shape[0], r)
-        pad = torch.zeros((self.maxrows, r), dtype=local.dtype, device=local.device)
-        pad[: loc2.shape[0]] = loc2
-        buf = torch.empty((self.world * self.maxrows, r), dtype=local.dtype, device=local.device)
-        dist.all_gather_into_tensor(buf, pad, group=self.group)
-        out = torch.cat([buf[i * self.maxrows: i * self.maxrows + (b - a)] for i, (a, b) in enumerate(self.shards)])
+        self.slot(r, local.dtype, local.device).copy_(local.reshape(local.shape[0], r))
+        out = self.gather_slot(r, local.dtype, local.device)
+        if self.equal:
+            out = out.clone()      # the buffer is reused by the next gather
         return out.reshape(self.n) if local.dim() == 1 else out
 
 
@@ -192,7 +221,32 @@ class ShardedOperator:
                             row_scale=self.rscale_q, row_div=self.ph, out_dtype=out_dtype)
         return out[:, 0] if squeeze else out
 
+    def _gather_dtype(self):
+        return torch.float32 if self.op.precision in ("f16", "bf16") else torch.float64
+
+    def matvec_shard(self, v: torch.Tensor):
+        """This rank's rows of the product, written by the tile kernel straight
+        into its chunk of the gather buffer (several GPUs), or returned (one)."""
+        if self.world == 1:
+            return self.matvec_local(v)
+        r = 1 if v.dim() == 1 else v.shape[1]
+        slot = self.gather.slot(r, self._gather_dtype(), v.device)
+        self.op.apply(v[:, None] if v.dim() == 1 else v, col_scale=self.rscale_k, col_h=self.h,
+                      row_scale=self.rscale_q, row_div=self.ph, out_dtype=slot.dtype, out=slot)
+        return slot
+
+    def gather_shards(self, shard: torch.Tensor, squeeze: bool) -> torch.Tensor:
+        """The all-gather that completes ``matvec_shard``: the full fp64 product."""
+        if self.world == 1:
+            return shard
+        r = shard.shape[1]
+        full = self.gather.gather_slot(r, shard.dtype, shard.device)
+        full = full.to(torch.float64) if full.dtype != torch.float64 else (full.clone() if self.gather.equal else full)
+        return full.reshape(self.nq) if squeeze else full
+
     def matvec_device(self, v: torch.Tensor) -> torch.Tensor:
-        """Full product on every rank: this rank's rows + one all-gather."""
-        return self.gather(self.matvec_local(v))
+        """Full product on every rank: this rank's rows + one all-gather.  The
+        16-bit tiles (error bound 2e-3) gather fp32, half the bytes of the fp64
+        that the fp32-class tiles gather; the result is fp64 either way."""
+        return self.gather_shards(self.matvec_shard(v), v.dim() == 1)
 

@@ -125,3 +125,47 @@ def test_rank_that_leaves_is_detected_by_the_next_gather():
     assert res[1][0] == "left"
     assert res[0][0] != "no error", res[0]
     assert res[0][1] < 60.0
+
+
+def _gather_worker(rank, world, port, n, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = RowGather(n, world)
+        a, b = g.shards[rank]
+        res = []
+        for step in range(2):                     # the buffer is reused between gathers
+            for dt in (torch.float32, torch.float64):
+                slot = g.slot(3, dt, torch.device("cpu"))
+                slot.copy_(torch.arange(a, b, dtype=dt)[:, None] * (step + 1) + torch.arange(3, dtype=dt))
+                full = g.gather_slot(3, dt, torch.device("cpu")).clone()
+                res.append(full.numpy())
+        first = g(torch.arange(a, b, dtype=torch.float32))
+        second = g(torch.arange(a, b, dtype=torch.float32) * 2)
+        out_q.put((rank, res, first.numpy(), second.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [512, 700])          # equal shards (views) and uneven shards (gather-copy)
+def test_row_gather_slots_in_place(n):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_gather_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(60)
+        assert p.exitcode == 0
+    rows = np.arange(n, dtype=np.float64)
+    for _, res, first, second in outs:
+        k = 0
+        for step in range(2):
+            for _dt in range(2):
+                want = rows[:, None] * (step + 1) + np.arange(3)
+                assert np.array_equal(res[k], want)
+                k += 1
+        assert np.array_equal(first, rows) and np.array_equal(second, 2 * rows)   # no aliasing
