@@ -47,7 +47,7 @@ def build_cuda(verbose=False, force=False, extra=()):
     if not force and not _stale(LIB, deps):
         return LIB
     cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp", *cu, *extra]
+           "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp", *cu, "-ldl", *extra]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)

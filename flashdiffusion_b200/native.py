@@ -49,6 +49,13 @@ SIGNATURES = {
     "fd_selftest_wait_timeout": (_I, [_L, _P]),
     "fd_set_exp2_fma_cols": (_I, [_I]),
     "fd_lanczos_workspace_bytes": (_S, [_L, _I]),
+    "fd_comm_id_bytes": (_S, []),
+    "fd_comm_get_id": (_I, [_P]),
+    "fd_comm_init": (_I, [_P, _P, _I, _I]),
+    "fd_comm_allgather": (_I, [_P, _P, _P, _S, _P]),
+    "fd_comm_check": (_I, [_P]),
+    "fd_comm_abort": (_I, [_P]),
+    "fd_comm_destroy": (_I, [_P]),
     "fd_lanczos_reorth": (_I, [_P, _L, _I, _L, _P, _P, _P, _P, _S, _P]),
     "fd_selftest_exp2_poly": (_I, [_P, _L, _P, _P]),
     "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
@@ -238,6 +245,43 @@ def lanczos_reorth(V: torch.Tensor, rows: int, w: torch.Tensor, out: torch.Tenso
     aligned = (base + 255) & ~255
     check(load().fd_lanczos_reorth(_ptr(V), V.stride(0), int(rows), V.shape[1], _ptr(w), _ptr(out), _ptr(coef),
                                    ctypes.c_void_p(aligned), ws.numel() - (aligned - base), _stream(V.device)))
+
+
+class Comm:
+    """The library's NCCL communicator (fd_comm_*), for hosts without torch.distributed.
+
+    ``Comm.new_id()`` on one rank; pass the bytes to every rank; ``Comm(id, nranks, rank)``."""
+
+    @staticmethod
+    def new_id() -> bytes:
+        lib = load()
+        buf = ctypes.create_string_buffer(int(lib.fd_comm_id_bytes()))
+        check(lib.fd_comm_get_id(buf))
+        return buf.raw
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        self.handle = ctypes.c_void_p()
+        check(load().fd_comm_init(ctypes.byref(self.handle), ctypes.create_string_buffer(uid, len(uid)),
+                                  int(nranks), int(rank)))
+        self.nranks, self.rank = nranks, rank
+
+    def allgather_(self, buf: torch.Tensor) -> torch.Tensor:
+        """In-place all-gather: chunk ``rank`` of the contiguous ``buf`` (split in nranks) to every rank."""
+        chunk = buf.numel() * buf.element_size() // self.nranks
+        send = ctypes.c_void_p(buf.data_ptr() + self.rank * chunk)
+        check(load().fd_comm_allgather(self.handle, send, _ptr(buf), chunk, _stream(buf.device)))
+        return buf
+
+    def check(self) -> None:
+        check(load().fd_comm_check(self.handle))
+
+    def abort(self) -> None:
+        check(load().fd_comm_abort(self.handle))
+        self.handle = ctypes.c_void_p()
+
+    def close(self) -> None:
+        check(load().fd_comm_destroy(self.handle))
+        self.handle = ctypes.c_void_p()
 
 
 def check_status(device=None) -> None:

@@ -196,6 +196,38 @@ int fd_lanczos_reorth(const double* V, int64_t ldv, int rows, int64_t n, double*
                       double* coef, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Multi-GPU collective of the row-sharded operator (no counterpart in the
+ * reference, which has no distributed code).  One process per GPU; rank r
+ * owns contiguous row shards of Q and holds all of K; after its tile pass it
+ * all-gathers the output shards over NVLink so every rank holds the whole
+ * product.  NCCL is opened at run time (libnccl.so.2); without it these
+ * return FD_ERR_UNSUPPORTED and the rest of the library is unaffected.
+ * ------------------------------------------------------------------------- */
+
+/* Size of the opaque rendezvous id (NCCL unique id), in bytes. */
+size_t fd_comm_id_bytes(void);
+
+/* Make a new rendezvous id on one rank (host memory of fd_comm_id_bytes());
+ * the caller hands it to every rank by its own means. */
+int fd_comm_get_id(void* id);
+
+/* Join communicator `rank` of `nranks` on the current device (blocking until
+ * every rank joined).  *comm receives an opaque handle. */
+int fd_comm_init(void** comm, const void* id, int nranks, int rank);
+
+/* recv[rank * bytes_per_rank ...] <- every rank's send (bytes_per_rank bytes
+ * each; send may be recv's own chunk, in place), ordered on `stream`. */
+int fd_comm_allgather(void* comm, const void* send, void* recv, size_t bytes_per_rank, void* stream);
+
+/* FD_OK, or FD_ERR_CUDA if the communicator recorded an asynchronous error
+ * (a peer that left, a network fault). */
+int fd_comm_check(void* comm);
+
+/* Abort (unblocks collectives in flight; for failure paths) or destroy. */
+int fd_comm_abort(void* comm);
+int fd_comm_destroy(void* comm);
+
+/* ---------------------------------------------------------------------------
  * Bandwidth selection (FD/utils.py:16-52), fp32 row-major inputs, fp32 CUDA-core
  * arithmetic on coordinate differences.
  * ------------------------------------------------------------------------- */

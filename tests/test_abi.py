@@ -104,3 +104,14 @@ def test_no_device_raises_loudly():
         native.require_device()
     with pytest.raises(RuntimeError):
         FlashDiffusion(np.ones((3, 2)), np.ones((3, 2)), np.ones((3, 1)), 1.0)
+
+
+def test_comm_rendezvous_id_without_a_gpu():
+    """fd_comm_get_id needs only NCCL's host side: an id of fd_comm_id_bytes() bytes."""
+    from flashdiffusion_b200 import native
+    lib = native.load()
+    n = int(lib.fd_comm_id_bytes())
+    assert n == 128
+    a, b = native.Comm.new_id(), native.Comm.new_id()
+    assert len(a) == n and a != b
+    assert lib.fd_comm_allgather(None, None, None, 0, None) == native.FD_ERR_ARG

@@ -35,6 +35,23 @@ def _worker(rank, world, port, X, h, out_q):
                                  h=torch.from_numpy(h).to(dev) if mode == "doob" else None).fit()
             v = torch.from_numpy(np.random.default_rng(1).standard_normal((X.shape[0], 3))).to(dev)
             res[mode] = op.matvec_device(v).cpu().numpy()
+        # LOBPCG on the sharded DMAP operator: every block product is row shards + one all-gather
+        from flashdiffusion_b200.eigensolver import SolveInfo, lobpcg_core
+        op = ShardedOperator(Xd, None, 0.05, 0.5, "f16", mode="dmap").fit()
+        vals, _ = lobpcg_core(lambda B: op.matvec_device(B), X.shape[0], 4, 1e-4, 80, 42, dev, SolveInfo(), guard=4)
+        res["lobpcg"] = np.asarray(vals)
+        # the library's own NCCL communicator (fd_comm_*), id handed over by torch.distributed
+        from flashdiffusion_b200 import native
+        ids = [native.Comm.new_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        comm = native.Comm(ids[0], world, rank)
+        buf = torch.zeros(world * 1000, dtype=torch.float64, device=dev)
+        buf[rank * 1000:(rank + 1) * 1000] = rank + 1.0
+        comm.allgather_(buf)
+        torch.cuda.synchronize()
+        comm.check()
+        comm.close()
+        res["comm"] = buf.cpu().numpy()
         out_q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -65,6 +82,14 @@ def test_two_gpu_row_shards_match_single_gpu():
         ref = op.matvec_device(v).cpu().numpy()
         assert np.array_equal(res[0][mode], res[1][mode])
         assert np.linalg.norm(res[0][mode] - ref) <= 1e-5 * np.linalg.norm(ref)
+    # sharded LOBPCG: identical on both ranks, and the top eigenvalues of the 1-GPU solve
+    from flashdiffusion_b200.eigensolver import SolveInfo, lobpcg_core
+    op = ShardedOperator(Xd, None, 0.05, 0.5, "f16", mode="dmap").fit()
+    vals, _ = lobpcg_core(lambda B: op.matvec_device(B), X.shape[0], 4, 1e-4, 80, 42, Xd.device, SolveInfo(), guard=4)
+    assert np.array_equal(res[0]["lobpcg"], res[1]["lobpcg"])
+    assert np.allclose(res[0]["lobpcg"], vals, rtol=1e-5)
+    for r in range(2):
+        assert np.array_equal(res[r]["comm"], np.repeat([1.0, 2.0], 1000))
     # DMAP product vs the oracle
     from oracle import fd_oracle as O
     _, _, rs = O.dmap_fit(X, 0.05, 0.5)
