@@ -145,11 +145,10 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
     if (nq == 0) return FD_OK;
 
     // (the workspace query is sized for block_max_cols columns, an upper bound for any d)
-    // block tensor-core path for r > 1 up to 208 operand columns; wider operands
-    // (the 128-row streaming kernel) take one column per launch
-    const bool wide = is_tc_tile(tile) && kd_tile(tile, d) > 208;
-    const bool block = is_tc_tile(tile) && r > 1 && !wide;
-    const int cpl = block ? block_max_cols(d) : (wide ? 1 : cols_per_launch(tile, r));
+    // block tensor-core path for every r > 1 (operand rows of up to 416 columns;
+    // above 208 the key tiles stream through the ring as single boxes)
+    const bool block = is_tc_tile(tile) && r > 1;
+    const int cpl = block ? block_max_cols(d) : cols_per_launch(tile, r);
     const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
     uint8_t* ws = (uint8_t*)workspace;
     float* u = (float*)ws;

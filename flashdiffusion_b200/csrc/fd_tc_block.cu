@@ -91,16 +91,22 @@ struct Cfg {
     static constexpr uint32_t UT_BOX = RP * 128;                 // RP rows x 64 keys
     // two rings: K tiles (released as soon as Q.K^T is done) and U^T tiles
     // (U_hi^T and U_lo^T, 2 boxes each; released after P.U, i.e. after the epilogue)
-    static constexpr uint32_t STAGE_BYTES = G::bytes(BN);
+    // Wide operands (fp32-class tiles of d = 68..136: rows of 224..416 columns):
+    // a whole key tile per ring stage would leave no room for a second stage,
+    // so the K ring holds single 64-column boxes (the narrow box in a slot of
+    // its own) and one issuer consumes them in order.
+    static constexpr bool WIDE = KF * 64 + NW > 208;
+    static constexpr uint32_t STAGE_BYTES = WIDE ? KBOX_BYTES : G::bytes(BN);
     static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX;
     static constexpr uint32_t BUDGET = 222u * 1024u - Q_BYTES;
     static constexpr uint32_t ACC_BYTES = RP * BM * 4;     // running O sums of the segment
     // U^T tiles live from their load to their P.U: 4 stages unless that leaves
-    // fewer than 3 K stages
+    // fewer than 3 K stages (2 for the wide operands)
     static constexpr int USTAGES =
-        (BUDGET - ACC_BYTES - 4 * USTAGE_BYTES) / STAGE_BYTES >= 3 ? 4 : 3;
+        WIDE ? 2 : ((BUDGET - ACC_BYTES - 4 * USTAGE_BYTES) / STAGE_BYTES >= 3 ? 4 : 3);
     static constexpr int K_RAW = (int)((BUDGET - ACC_BYTES - USTAGES * USTAGE_BYTES) / STAGE_BYTES);
-    static constexpr int STAGES = K_RAW > 6 ? 6 : (K_RAW < 2 ? 2 : K_RAW);
+    static constexpr int STAGES = K_RAW > (WIDE ? 8 : 6) ? (WIDE ? 8 : 6) : (K_RAW < 2 ? 2 : K_RAW);
+    static_assert(!WIDE || STAGES >= 3, "wide operands need at least 3 box slots");
     static constexpr uint32_t U_OFF = Q_BYTES + STAGES * STAGE_BYTES;
     static constexpr uint32_t ACC_OFF = U_OFF + USTAGES * USTAGE_BYTES;
     static constexpr uint32_t BAR_OFF = ACC_OFF + ACC_BYTES;
@@ -227,7 +233,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             ptx::mbar_init(&uempty[i], 2);   // both P.U issuers
         }
         ptx::mbar_init(qfull, 1);
-        ptx::mbar_init(qempty, 2);          // both Q.K^T issuers
+        ptx::mbar_init(qempty, C::WIDE ? 1 : 2);   // both Q.K^T issuers (one for wide operands)
         for (int i = 0; i < NSB; ++i) {
             ptx::mbar_init(&sfull[i], 1);
             ptx::mbar_init(&sempty[i], 2);   // both P.U issuers
@@ -270,13 +276,31 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     cur_rt = rt;
                     ++qcount;
                 }
-                if (!FD_WAIT(1, &kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
-                uint8_t* st = sK + stage * C::STAGE_BYTES;
-                ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
-                for (int kb = 0; kb < KF; ++kb)
-                    ptx::tma_load_2d(st + kb * KBOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
-                if (NW) ptx::tma_load_2d(st + KF * KBOX_BYTES, &tmk_n, &kfull[stage], KF * 64, (int)(jt * BN));
-                if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                if constexpr (C::WIDE) {
+                    // one box per ring slot, in column order
+                    bool ok = true;
+                    for (int kb = 0; kb < KF + (NW ? 1 : 0) && ok; ++kb) {
+                        if (!FD_WAIT(1, &kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                        uint8_t* st = sK + stage * C::STAGE_BYTES;
+                        if (kb < KF) {
+                            ptx::mbar_expect_tx(&kfull[stage], KBOX_BYTES);
+                            ptx::tma_load_2d(st, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                        } else {
+                            ptx::mbar_expect_tx(&kfull[stage], BN * NW * 2);
+                            ptx::tma_load_2d(st, &tmk_n, &kfull[stage], KF * 64, (int)(jt * BN));
+                        }
+                        if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                    }
+                    if (!ok) break;
+                } else {
+                    if (!FD_WAIT(1, &kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
+                    uint8_t* st = sK + stage * C::STAGE_BYTES;
+                    ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
+                    for (int kb = 0; kb < KF; ++kb)
+                        ptx::tma_load_2d(st + kb * KBOX_BYTES, &tmk, &kfull[stage], kb * 64, (int)(jt * BN));
+                    if (NW) ptx::tma_load_2d(st + KF * KBOX_BYTES, &tmk_n, &kfull[stage], KF * 64, (int)(jt * BN));
+                    if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                }
             }
         }
     } else if (warp == UTMA_WARP) {
@@ -305,13 +329,42 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
-            for (Walk w(sc, cta); !w.done(); w.next()) {
+            for (Walk w(sc, cta); !w.done() && !(C::WIDE && q == 1); w.next()) {
                 const int64_t m = w.s, rt = w.rt;
                 const int b = (int)(m % NSB);
                 if (rt != cur_rt) {
                     if (!FD_WAIT(6, qfull, qcount & 1, abort, status, WAIT_LIMIT_NS)) break;
                     ++qcount;
                     cur_rt = rt;
+                }
+                if constexpr (C::WIDE) {
+                    // one issuer, every tile; the key boxes arrive one per ring slot
+                    if (!FD_WAIT(8, &sempty[b], (uint32_t)(((m / NSB) & 1) ^ 1), abort, status, WAIT_LIMIT_NS)) break;
+                    bool ok = true;
+                    int ks = 0;
+                    for (int kb = 0; kb < KF + (NW ? 1 : 0); ++kb) {
+                        if (!FD_WAIT(7, &kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t ka = k_base + stage * C::STAGE_BYTES;
+                        if (kb < KF) {
+#pragma unroll
+                            for (int k4 = 0; k4 < 4; ++k4, ++ks)
+                                ptx::umma_ss(tmem + b * BN, G::desc(q_base, BM, ks), ptx::sw128_kmajor_desc(ka + k4 * 32),
+                                             idesc_qk, ks > 0);
+                        } else {
+                            for (int k2 = 0; k2 < NW / 16; ++k2, ++ks) {
+                                const uint64_t bd = NW == 32 ? ptx::sw64_kmajor_desc(ka + k2 * 32)
+                                                             : ptx::sw32_kmajor_desc(ka + k2 * 32);
+                                ptx::umma_ss(tmem + b * BN, G::desc(q_base, BM, ks), bd, idesc_qk, ks > 0);
+                            }
+                        }
+                        ptx::umma_commit(&kempty[stage]);
+                        if (++stage == C::STAGES) { stage = 0; kph ^= 1; }
+                    }
+                    if (!ok) break;
+                    ptx::umma_commit(&sfull[b]);
+                    if (w.seg_last()) ptx::umma_commit(qempty);
+                    continue;
                 }
                 if ((int)(m & 1) == q) {
                     if (!FD_WAIT(7, &kfull[stage], kph, abort, status, WAIT_LIMIT_NS)) break;
@@ -601,7 +654,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     const int kd = kd_tile(tile, d);
     int kf = 0, nw = 0;
     split_kd(kd, &kf, &nw);
-    if (kd > 208) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 208)", kd);
+    if (kd > 416) return set_error(FD_ERR_UNSUPPORTED, "tensor-core tile path: operand rows of %d columns (max 416)", kd);
     const size_t need = tc_block_workspace_bytes(rp);
     if (ws_bytes < need)
         return set_error(FD_ERR_WORKSPACE, "block tile path: workspace %zu B < %zu B", ws_bytes, need);
@@ -637,6 +690,16 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
         case 232: FD_TRY((launch_block_kb<2, 32>(rp, a, s))); break;
         case 300: FD_TRY((launch_block_kb<3, 0>(rp, a, s))); break;
         case 316: FD_TRY((launch_block_kb<3, 16>(rp, a, s))); break;
+        case 332: FD_TRY((launch_block_kb<3, 32>(rp, a, s))); break;
+        case 400: FD_TRY((launch_block_kb<4, 0>(rp, a, s))); break;
+        case 416: FD_TRY((launch_block_kb<4, 16>(rp, a, s))); break;
+        case 432: FD_TRY((launch_block_kb<4, 32>(rp, a, s))); break;
+        case 500: FD_TRY((launch_block_kb<5, 0>(rp, a, s))); break;
+        case 516: FD_TRY((launch_block_kb<5, 16>(rp, a, s))); break;
+        case 532: FD_TRY((launch_block_kb<5, 32>(rp, a, s))); break;
+        case 600: FD_TRY((launch_block_kb<6, 0>(rp, a, s))); break;
+        case 616: FD_TRY((launch_block_kb<6, 16>(rp, a, s))); break;
+        case 632: FD_TRY((launch_block_kb<6, 32>(rp, a, s))); break;
         default: return set_error(FD_ERR_UNSUPPORTED, "block tile path: no kernel for kd=%d", kd);
     }
     tcb::tc_block_fixup_kernel<<<(unsigned)cdiv(nq, tcb::BM), 256, 0, s>>>(a.part, a.sc, nq, rc, rp, ep);

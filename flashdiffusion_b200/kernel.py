@@ -77,7 +77,11 @@ def tile_of(precision=None, coord_dtype=np.float32) -> int:
     cd = np.dtype(coord_dtype) if not isinstance(coord_dtype, torch.dtype) else coord_dtype
     if cd in (np.dtype(np.float16), torch.float16):
         return native.TILE_F16
-    return native.TILE_F32
+    # fp32 coordinates (the reference default): the fp32-class tensor-core
+    # tiles, which meet the fp32 tiles' 1e-5 bound at the tensor-core rate; the
+    # operator falls back to the fp32 SIMT tiles where they do not apply
+    # (d > 136, or split values outside the fp16 range)
+    return native.TILE_F16X3
 
 
 PREC_OF_TILE = {v: k for k, v in TILE_NAMES.items()}

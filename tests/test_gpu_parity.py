@@ -419,6 +419,47 @@ def test_c5_full_size_properties():
     assert rel_l2(out[rows], ref) <= TOL["f16"]
 
 
+@pytest.mark.parametrize("d,nq,nk,r", [(128, 3000, 40_000, 32), (100, 1000, 9_001, 5), (136, 700, 5_000, 17),
+                                       (70, 513, 3_000, 2)])
+def test_f16x3_block_product_wide_operands_vs_exact(d, nq, nk, r):
+    """fp32-class tiles with operand rows of 224..416 columns and a block right-hand side:
+    one block-kernel pass (the key tiles streamed box by box), held to the fp32-tile bound
+    1e-5 per column against exact fp64 sums."""
+    from flashdiffusion_b200 import GaussianOperator
+    rng = np.random.default_rng(d + r)
+    K = rng.standard_normal((nk, d)).astype(np.float32)
+    Q = (K[:nq] + 0.1 * rng.standard_normal((nq, d))).astype(np.float32)
+    beta = 1.0 / (2 * d)
+    V = rng.standard_normal((nk, r))
+    V[:, 0] = 1.0 + 0.01 * V[:, 0]
+    rk = rng.uniform(0.5, 2.0, nk).astype(np.float32)
+    op = GaussianOperator(Q, K, beta, "f16x3")
+    assert op.precision == "f16x3"
+    out = op.apply(torch.from_numpy(V).cuda(), col_scale=torch.from_numpy(rk).cuda(),
+                   out_dtype=torch.float64).cpu().numpy()
+    rows = np.arange(0, nq, max(1, nq // 60))
+    Qr, Kf = Q[rows].astype(np.float64), K.astype(np.float64)
+    d2 = (Qr ** 2).sum(1)[:, None] + (Kf ** 2).sum(1)[None, :] - 2.0 * Qr @ Kf.T
+    ref = np.exp(-beta * np.maximum(d2, 0.0)) @ (V * rk[:, None])
+    for c in range(r):
+        assert rel_l2(out[rows, c], ref[:, c]) <= TOL["f16x3"], c
+
+
+def test_default_coord_dtype_uses_fp32_class_tensor_cores():
+    """The reference's default coord_dtype=np.float32 runs the f16x3 tensor-core tiles and
+    meets the fp32-tile bound."""
+    from flashdiffusion_b200 import FlashDiffusion
+    from flashdiffusion_b200.kernel import GaussianOperator, tile_of
+    from flashdiffusion_b200 import native
+    assert tile_of(None, np.float32) == native.TILE_F16X3
+    rng = np.random.default_rng(3)
+    X = rng.standard_normal((2000, 64)).astype(np.float32)
+    V = rng.standard_normal((2000, 3))
+    out = FlashDiffusion(X, X, V, 1.0 / 128)
+    assert rel_l2(out, exact_apply(X, X, V, 1.0 / 128)) <= 1e-5
+    assert GaussianOperator(X, None, 1.0 / 128, "f16x3").precision == "f16x3"
+
+
 def test_c5_full_size_block_product():
     """Configuration 5's block product at 1M points (d=128, r=32, one tcgen05 block-kernel pass
     with the DMAP scales): every column on a seeded row subset against exact fp64 sums over all
