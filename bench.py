@@ -407,6 +407,28 @@ def run_ours(args):
         lanczos = {"k": kk, "operator": emode, "seconds": float(lt.item()), "n_matvec": info.n_matvec, "tol": 1e-7,
                    "stages": info.stages, "max_rel_residual": info.stages[-1]["max_rel_residual"],
                    "top_eigenvalues": [float(x) for x in vals[:4]]}
+        # the Lanczos vector operations alone: one full reorthogonalisation
+        # step (fd_lanczos_reorth) against a basis of ncv rows, HBM bytes =
+        # three reads of the basis + the vectors, over CUDA-event time
+        ncv = min(max(2 * kk + 1, 20), nq)
+        Vb = torch.randn((ncv + 1, nq), dtype=torch.float64, device=dev)
+        wv = torch.randn(nq, dtype=torch.float64, device=dev)
+        cf = torch.zeros(ncv + 2, dtype=torch.float64, device=dev)
+        wsz = native.lanczos_workspace(nq, ncv, dev)
+        for _ in range(3):
+            native.lanczos_reorth(Vb, ncv, wv, Vb[ncv], cf, wsz)
+        flush.zero_()
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        for _ in range(10):
+            native.lanczos_reorth(Vb, ncv, wv, Vb[ncv], cf, wsz)
+        b_.record()
+        torch.cuda.synchronize()
+        rt_ms = a_.elapsed_time(b_) / 10
+        rbytes = 8.0 * (3 * ncv * nq + 5 * nq)
+        lanczos["reorth"] = {"rows": ncv, "n": nq, "ms": rt_ms, "bytes": rbytes,
+                             "achieved_gbs": rbytes / (rt_ms / 1e3) / 1e9,
+                             "basis_bytes": 8.0 * ncv * nq}
 
     # configuration 5: k = 32 eigenpairs by LOBPCG whose block products are single
     # r = 32 passes of the tensor-core block kernel (16-bit tiles): stage 1 with
@@ -450,6 +472,9 @@ def run_ours(args):
     mufu_peak = 16 * 148 * sm_max * 1e6          # ex2 per s at max SM clock (measured 15.9/clk/SM)
     tensor_peak_evals = bf16_tf * 1e12 / flops_per_eval
     peak_evals = min(mufu_peak, tensor_peak_evals)
+    if lanczos is not None and "reorth" in lanczos:
+        lanczos["reorth"]["peak_gbs"] = hbm
+        lanczos["reorth"]["frac"] = lanczos["reorth"]["achieved_gbs"] / hbm
     if lanczos is not None:
         # the eigensolve against the same roofline: every product at the roofline rate
         # (Lanczos: r = 1 products; LOBPCG: r-column block products, block_columns / r of them)
