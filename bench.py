@@ -63,6 +63,9 @@ def parse():
     p.add_argument("--no-lobpcg", action="store_true", help="block configurations: skip LOBPCG to k = r eigenpairs")
     p.add_argument("--lobpcg-tol", type=float, default=1e-3)
     p.add_argument("--lobpcg-tol2", type=float, default=1e-5)
+    p.add_argument("--lobpcg-final", default="f16", choices=["f16", "f16x3"],
+                   help="tiles of the last LOBPCG stage: 16-bit with one key tile per accumulation group, or the "
+                        "fp32-class tiles (the precision ramp; pair with --lobpcg-tol2 1e-7)")
     p.add_argument("--tiles", default="f16", choices=["f16", "bf16", "f16x3", "fp32"],
                    help="tile precision of the timed operator (default the 16-bit fp16 tiles)")
     a = p.parse_args()
@@ -444,9 +447,14 @@ def run_ours(args):
             info = SolveInfo()
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            vals, X = lobpcg_core(lambda B: op.matvec_device(B), nq, r, tol, 60, 42, dev, info, guard=16, X0=X)
+            sop = op
+            if group == 1 and args.lobpcg_final == "f16x3":
+                # the ramp's fp32-class stage: block products on the split-operand tiles
+                sop = ShardedOperator(Qd, Kd, beta, 0.5, "f16x3", mode=cfg["mode"], h=hd).fit()
+            vals, X = lobpcg_core(lambda B: sop.matvec_device(B), nq, r, tol, 60, 42, dev, info, guard=16, X0=X)
             torch.cuda.synchronize()
-            stages.append({"key_tiles_per_group": group or 8, "tol": tol, "seconds": time.perf_counter() - t0,
+            stages.append({"key_tiles_per_group": group or 8, "tiles": sop.op.precision, "tol": tol,
+                           "seconds": time.perf_counter() - t0,
                            "block_columns_applied": info.n_matvec, "iterations": info.n_restart,
                            "converged": info.converged, "max_rel_residual": float(np.max(info.residuals)),
                            "top_eigenvalues": [float(x) for x in vals[:4]]})
@@ -454,7 +462,7 @@ def run_ours(args):
         lt = torch.tensor([time.perf_counter() - t00], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(lt, op=dist.ReduceOp.MAX)
-        lanczos = {"k": r, "method": "LOBPCG (16 guard columns), 16-bit block tiles, two stages",
+        lanczos = {"k": r, "method": "LOBPCG (16 guard columns), block tiles, two stages",
                    "seconds": float(lt.item()), "stages": stages,
                    "max_rel_residual": stages[-1]["max_rel_residual"], "top_eigenvalues": [float(x) for x in vals[:4]]}
 
