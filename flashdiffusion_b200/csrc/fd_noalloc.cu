@@ -74,7 +74,8 @@ extern "C" int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, in
     FD_TRY(noalloc_scratch(&scratch));
     // Nothing in the scratch has to start at zero: the right-hand side region
     // (including its zero padding) and every partial-sum slot the fix-up pass
-    // reads are written earlier in the same call.
+    // reads are written earlier in the same call, and the tile launch clears
+    // its lockstep pacing counter itself.
     return fd_apply(Qop, nq, Kop, nk, d, tile, V, v_dtype, r, col_scale, col_h, row_scale, row_div, out,
                     out_dtype, scratch, (size_t)FD_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -174,6 +174,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     cur_rt = rt;
                     ++qcount;
                 }
+                pace(sc, m, jt, abort);
                 if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
                 for (int kb = 0; kb < KF; ++kb)
@@ -667,9 +668,16 @@ int num_sms() {
     return n;
 }
 
+// cross-CTA partials, then one 256-byte line for the lockstep pacing counter
 size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
     (void)nq; (void)nk; (void)rc;
-    return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS);
+    return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS) + 256;
+}
+
+// Key tiles per pacing chunk: about 12 MB of key-side bytes.
+int64_t pace_tiles(size_t bytes_per_key_tile) {
+    const int64_t t = (int64_t)((12u << 20) / (bytes_per_key_tile ? bytes_per_key_tile : 1));
+    return t < 8 ? 8 : t;
 }
 
 struct TcArgs {
@@ -803,6 +811,11 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
     a.idesc = ptx::idesc_f32acc(tc::BM, tc::BN, f16);
     a.sc = tc::Sched::make(cdiv(nq, tc::ROWS), cdiv(nk, tc::BN), num_sms(), (size_t)nk * kd * 2);
     a.part = (double*)ws;
+    if (a.sc.full > 0) {
+        a.sc.sync = (unsigned*)((uint8_t*)ws + need - 256);
+        a.sc.pace_tiles = pace_tiles((size_t)tc::BN * kd * 2 + tc::BN * 4);
+        FD_CUDA_TRY(cudaMemsetAsync(a.sc.sync, 0, sizeof(unsigned), s));
+    }
     a.u = (const float*)rhs;
     a.nq = nq;
     a.ep = ep;

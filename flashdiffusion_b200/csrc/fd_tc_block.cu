@@ -276,6 +276,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     cur_rt = rt;
                     ++qcount;
                 }
+                tc::pace(sc, w.s, jt, abort);
                 if constexpr (C::WIDE) {
                     // one box per ring slot, in column order
                     bool ok = true;
@@ -582,8 +583,9 @@ __global__ void tc_block_fixup_kernel(const double* __restrict__ part, Sched sc,
 
 int block_rp(int rc) { return rc <= 16 ? 16 : (rc <= 32 ? 32 : 64); }
 
+// cross-CTA partials, then one 256-byte line for the lockstep pacing counter
 size_t tc_block_workspace_bytes(int rp) {
-    return align256(sizeof(double) * 2 * (size_t)num_sms() * tcb::BM * rp);
+    return align256(sizeof(double) * 2 * (size_t)num_sms() * tcb::BM * rp) + 256;
 }
 
 struct BlockArgs {
@@ -673,6 +675,11 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     a.ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
     a.sc = tc::Sched::make(cdiv(nq, tcb::BM), cdiv(nk, tcb::BN), num_sms(), (size_t)nk * kd * 2);
     a.part = (double*)ws;
+    if (a.sc.full > 0) {
+        a.sc.sync = (unsigned*)((uint8_t*)ws + need - 256);
+        a.sc.pace_tiles = pace_tiles((size_t)tcb::BN * kd * 2 + (size_t)4 * tcb::BN * rp);
+        FD_CUDA_TRY(cudaMemsetAsync(a.sc.sync, 0, sizeof(unsigned), s));
+    }
     a.colscale = colscale;
     a.rc = rc;
     a.nq = nq;

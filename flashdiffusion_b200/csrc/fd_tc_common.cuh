@@ -46,6 +46,10 @@ struct Sched {
     int64_t n_rem;   // lockstep mode: remainder row tiles
     int k;           // lockstep mode: key chunks per remainder row (0 = contiguous mode)
     int grid;
+    // pacing of the lockstep sweeps (see pace()): a zeroed global counter and
+    // the key tiles per pacing chunk; null = no pacing
+    unsigned* sync = nullptr;
+    int64_t pace_tiles = 0;
     __host__ __device__ int64_t start(int c) const { return (int64_t)c * units / grid; }   // remainder range
     __host__ __device__ int64_t rem_rt0() const { return full * grid; }
     __host__ __device__ int64_t chunk0(int j) const { return (int64_t)j * n_jt / k; }
@@ -66,6 +70,32 @@ struct Sched {
         return sc;
     }
 };
+
+// Lockstep pacing.  The lockstep schedule only saves DRAM traffic while the
+// CTAs sweeping K stay within the L2's reach of each other, and over ~100
+// sweeps (configuration 5 at 2M points) they drift apart until every CTA
+// streams K from DRAM (measured: 8.5 TB per launch, 3.4 TB/s, which lowers the
+// power-capped clock).  So the key producer of every CTA, at the start of each
+// chunk of pace_tiles key tiles of a whole-row sweep, counts itself in a global
+// counter and waits until every CTA has started the chunk before: the CTAs
+// then stay within about two chunks (a few tens of MB) of each other.  The wait
+// is a hint, not a barrier: it gives up after 200 microseconds (a CTA that is
+// not resident yet cannot hold the others) or when the kernel aborts.
+__device__ __forceinline__ void pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort) {
+    if (sc.sync == nullptr || s >= sc.full * sc.n_jt || jt % sc.pace_tiles != 0) return;
+    const int64_t nchunk = (sc.n_jt + sc.pace_tiles - 1) / sc.pace_tiles;
+    const int64_t g = (s / sc.n_jt) * nchunk + jt / sc.pace_tiles;
+    atomicAdd(sc.sync, 1u);
+    const uint64_t target = (uint64_t)sc.grid * (uint64_t)g;
+    if (*(volatile unsigned*)sc.sync >= target) return;
+    const uint64_t t0 = ptx::globaltimer();
+    while (*(volatile unsigned*)sc.sync < target) {
+        if (*abort || ptx::globaltimer() - t0 > 200000ull) return;
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 700
+        __nanosleep(256);
+#endif
+    }
+}
 
 // One CTA's units in processing order (the same sequence in every role).  The
 // schedule's own fields are read from the kernel parameter, not copied, to keep
@@ -188,5 +218,7 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
 // kd = 64 kf + nw with nw in {0, 16, 32} (a remainder of 48 takes a full box).
 void split_kd(int kd, int* kf, int* nw);
 int num_sms();
+// Key tiles per lockstep pacing chunk for a key tile of this many bytes (key operand + right-hand side).
+int64_t pace_tiles(size_t bytes_per_key_tile);
 
 }  // namespace fd
