@@ -159,6 +159,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             int stage = 0;
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
+            bool pacing = true;
             for (Walk w(sc, cta); !w.done(); w.next()) {
                 const int64_t m = w.s, rt = w.rt, jt = w.jt;
                 if (rt != cur_rt) {
@@ -174,7 +175,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     cur_rt = rt;
                     ++qcount;
                 }
-                pace(sc, m, jt, abort);
+                if (pacing) pacing = pace(sc, m, jt, abort);
                 if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
                 for (int kb = 0; kb < KF; ++kb)
@@ -674,9 +675,9 @@ size_t tc_workspace_bytes(int64_t nq, int64_t nk, int rc) {
     return align256(sizeof(double) * 2 * (size_t)num_sms() * tc::ROWS) + 256;
 }
 
-// Key tiles per pacing chunk: about 12 MB of key-side bytes.
+// Key tiles per pacing chunk: about 8 MB of key-side bytes.
 int64_t pace_tiles(size_t bytes_per_key_tile) {
-    const int64_t t = (int64_t)((12u << 20) / (bytes_per_key_tile ? bytes_per_key_tile : 1));
+    const int64_t t = (int64_t)((8u << 20) / (bytes_per_key_tile ? bytes_per_key_tile : 1));
     return t < 8 ? 8 : t;
 }
 

@@ -78,23 +78,25 @@ struct Sched {
 // power-capped clock).  So the key producer of every CTA, at the start of each
 // chunk of pace_tiles key tiles of a whole-row sweep, counts itself in a global
 // counter and waits until every CTA has started the chunk before: the CTAs
-// then stay within about two chunks (a few tens of MB) of each other.  The wait
-// is a hint, not a barrier: it gives up after 200 microseconds (a CTA that is
-// not resident yet cannot hold the others) or when the kernel aborts.
-__device__ __forceinline__ void pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort) {
-    if (sc.sync == nullptr || s >= sc.full * sc.n_jt || jt % sc.pace_tiles != 0) return;
+// then stay within about two chunks of each other.  The wait is a hint, not a
+// barrier: after 5 ms (a CTA that is not resident cannot hold the others) or
+// when the kernel aborts it gives up and returns false, and the caller stops
+// pacing for the rest of the launch.
+__device__ __forceinline__ bool pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort) {
+    if (sc.sync == nullptr || s >= sc.full * sc.n_jt || jt % sc.pace_tiles != 0) return true;
     const int64_t nchunk = (sc.n_jt + sc.pace_tiles - 1) / sc.pace_tiles;
     const int64_t g = (s / sc.n_jt) * nchunk + jt / sc.pace_tiles;
     atomicAdd(sc.sync, 1u);
     const uint64_t target = (uint64_t)sc.grid * (uint64_t)g;
-    if (*(volatile unsigned*)sc.sync >= target) return;
+    if (*(volatile unsigned*)sc.sync >= target) return true;
     const uint64_t t0 = ptx::globaltimer();
     while (*(volatile unsigned*)sc.sync < target) {
-        if (*abort || ptx::globaltimer() - t0 > 200000ull) return;
+        if (*abort || ptx::globaltimer() - t0 > 5000000ull) return false;
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 700
-        __nanosleep(256);
+        __nanosleep(128);
 #endif
     }
+    return true;
 }
 
 // One CTA's units in processing order (the same sequence in every role).  The
@@ -218,7 +220,7 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
 // kd = 64 kf + nw with nw in {0, 16, 32} (a remainder of 48 takes a full box).
 void split_kd(int kd, int* kf, int* nw);
 int num_sms();
-// Key tiles per lockstep pacing chunk for a key tile of this many bytes (key operand + right-hand side).
+// Key tiles per lockstep pacing chunk (about 8 MB) for a key tile of this many bytes (key operand + right-hand side).
 int64_t pace_tiles(size_t bytes_per_key_tile);
 
 }  // namespace fd
