@@ -160,6 +160,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
             bool pacing = true;
+            int64_t paced = -1;
             for (Walk w(sc, cta); !w.done(); w.next()) {
                 const int64_t m = w.s, rt = w.rt, jt = w.jt;
                 if (rt != cur_rt) {
@@ -175,7 +176,7 @@ tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUten
                     cur_rt = rt;
                     ++qcount;
                 }
-                if (pacing) pacing = pace(sc, m, jt, abort);
+                if (pacing) pacing = pace(sc, m, jt, abort, paced);
                 if (!ptx::wait_bounded(&kempty[stage], kph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 ptx::mbar_expect_tx(&kfull[stage], C::STAGE_BYTES);
                 for (int kb = 0; kb < KF; ++kb)
@@ -440,6 +441,8 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
     if (warp == w::TMA_WARP || warp == w::TMA_WARP_ODD) {
         if (lane == 0) {
             const int pp = warp == w::TMA_WARP ? 0 : 1;   // this producer's tile parity
+            bool pacing = true;                            // (the even-tile producer paces)
+            int64_t paced = -1;
             uint32_t qcount = 0;
             int64_t cur_rt = -1;
             for (Walk wk(sc, cta); !wk.done(); wk.next()) {
@@ -454,6 +457,7 @@ tcw_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUte
                     ++qcount;
                 }
                 if ((int)(m & 1) != pp) continue;
+                if (pp == 0 && pacing) pacing = pace(sc, m, jt, abort, paced);
                 bool ok = true;
                 for (int kb = 0; kb < C::NB; ++kb) {
                     // position in this pipeline's sub-ring, consumed in order by one issuer
@@ -765,6 +769,11 @@ static int launch_tc_wide(const void* qop, int64_t nq, const void* kop, int64_t 
     a.idesc = ptx::idesc_f32acc(tc::w::BM, tc::w::BN, f16);
     a.sc = tc::Sched::make(cdiv(nq, tc::w::BM), cdiv(nk, tc::w::BN), num_sms(), (size_t)nk * kd * 2);
     a.part = (double*)ws;
+    if (a.sc.full > 0) {
+        a.sc.sync = (unsigned*)((uint8_t*)ws + need - 256);
+        a.sc.pace_tiles = pace_tiles((size_t)tc::w::BN * kd * 2 + tc::w::BN * 4);
+        FD_CUDA_TRY(cudaMemsetAsync(a.sc.sync, 0, sizeof(unsigned), s));
+    }
     a.u = (const float*)rhs;
     a.nq = nq;
     a.ep = ep;

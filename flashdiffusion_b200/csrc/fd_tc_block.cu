@@ -266,6 +266,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             uint32_t kph = 0, qcount = 0;
             int64_t cur_rt = -1;
             bool pacing = true;
+            int64_t paced = -1;
             for (Walk w(sc, cta); !w.done(); w.next()) {
                 const int64_t rt = w.rt, jt = w.jt;
                 if (rt != cur_rt) {
@@ -277,7 +278,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     cur_rt = rt;
                     ++qcount;
                 }
-                if (pacing) pacing = tc::pace(sc, w.s, jt, abort);
+                if (pacing) pacing = tc::pace(sc, w.s, jt, abort, paced);
                 if constexpr (C::WIDE) {
                     // one box per ring slot, in column order
                     bool ok = true;

@@ -82,10 +82,14 @@ struct Sched {
 // barrier: after 5 ms (a CTA that is not resident cannot hold the others) or
 // when the kernel aborts it gives up and returns false, and the caller stops
 // pacing for the rest of the launch.
-__device__ __forceinline__ bool pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort) {
-    if (sc.sync == nullptr || s >= sc.full * sc.n_jt || jt % sc.pace_tiles != 0) return true;
+// Called for the units a producer loads (every unit, or every other one);
+// `last` (start at -1) remembers the chunk last counted.
+__device__ __forceinline__ bool pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort, int64_t& last) {
+    if (sc.sync == nullptr || s >= sc.full * sc.n_jt) return true;
     const int64_t nchunk = (sc.n_jt + sc.pace_tiles - 1) / sc.pace_tiles;
     const int64_t g = (s / sc.n_jt) * nchunk + jt / sc.pace_tiles;
+    if (g == last) return true;
+    last = g;
     atomicAdd(sc.sync, 1u);
     const uint64_t target = (uint64_t)sc.grid * (uint64_t)g;
     if (*(volatile unsigned*)sc.sync >= target) return true;
