@@ -79,9 +79,10 @@ struct Sched {
 // chunk of pace_tiles key tiles of a whole-row sweep, counts itself in a global
 // counter and waits until every CTA has started the chunk before: the CTAs
 // then stay within about two chunks of each other.  The wait is a hint, not a
-// barrier: after 5 ms (a CTA that is not resident cannot hold the others) or
-// when the kernel aborts it gives up and returns false, and the caller stops
-// pacing for the rest of the launch.
+// barrier: it gives up after 1 ms (a CTA that is not resident yet cannot hold
+// the others for longer; measured, giving up for good after one such wait let
+// the sweeps drift apart again under the profiler) and returns false only when
+// the kernel aborts, which ends the pacing of that producer.
 // Called for the units a producer loads (every unit, or every other one);
 // `last` (start at -1) remembers the chunk last counted.
 __device__ __forceinline__ bool pace(const Sched& sc, int64_t s, int64_t jt, volatile int* abort, int64_t& last) {
@@ -95,7 +96,8 @@ __device__ __forceinline__ bool pace(const Sched& sc, int64_t s, int64_t jt, vol
     if (*(volatile unsigned*)sc.sync >= target) return true;
     const uint64_t t0 = ptx::globaltimer();
     while (*(volatile unsigned*)sc.sync < target) {
-        if (*abort || ptx::globaltimer() - t0 > 5000000ull) return false;
+        if (*abort) return false;
+        if (ptx::globaltimer() - t0 > 1000000ull) return true;
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 700
         __nanosleep(128);
 #endif
