@@ -215,7 +215,7 @@ class ClockSampler:
 # (dram__bytes_read.sum + dram__bytes_write.sum; the capture commands are in
 # the named profile summaries).
 TRAFFIC = {"c2": (69.3e6, "profiles/tc_kernel_c2_dmap_matvec.md"),
-           "c5r1": (9.71e9, "profiles/tc_kernel_c5r1_dmap_matvec.md")}
+           "c5": (661.2e9, "profiles/tc_block_kernel_c5_2m_traffic.md")}
 
 
 def load_peaks():
