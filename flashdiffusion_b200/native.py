@@ -60,6 +60,8 @@ SIGNATURES = {
     "fd_selftest_exp2_poly": (_I, [_P, _L, _P, _P]),
     "fd_knn_sqdist": (_I, [_P, _L, _P, _L, _I, _I, _P, _P]),
     "fd_pairwise_sqdist": (_I, [_P, _L, _I, _P, _P]),
+    "fd_knn_tc_workspace_bytes": (_S, [_L, _L, _I, _I]),
+    "fd_knn_sqdist_tc": (_I, [_P, _L, _P, _L, _I, _I, _P, _P, _S, _P]),
     "fd_rope_windows": (_I, [_P, _L, _L, _P, _L, _L, _L, _I, _I, _I, _I, ctypes.c_double, _P, _I, _P, _P, _P,
                              _P]),
 }

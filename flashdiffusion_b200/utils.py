@@ -4,7 +4,8 @@
 and return values; the O(m^2) / O(N^2) distance work runs in libfd_sm100.so
 (``fd_pairwise_sqdist``, ``fd_knn_sqdist``: fp32 coordinate differences on the
 CUDA cores, the k smallest per row kept in registers, so no N x N matrix is
-formed or sorted).  The seeded subsample of the median rule is drawn on the host
+formed or sorted; ``fd_knn_sqdist_tc``: every pair screened on the tensor cores,
+the candidates refined with the same exact arithmetic).  The seeded subsample of the median rule is drawn on the host
 exactly as the reference draws it.
 """
 
@@ -39,15 +40,33 @@ def median_bandwidth(X, subsample: int = 2000) -> float:
     return 1.0 / (2.0 * med) if med > 0 else 1.0
 
 
-def knn_sqdist(Q, K=None, k: int = 8) -> torch.Tensor:
-    """(N_q, k) device fp32: the k smallest squared distances of each query row to the keys, ascending."""
+def knn_sqdist(Q, K=None, k: int = 8, method: str = "auto") -> torch.Tensor:
+    """(N_q, k) device fp32: the k smallest squared distances of each query row to the keys, ascending.
+
+    ``method``: "tc" screens every pair on the tensor cores and refines the
+    candidates exactly (``fd_knn_sqdist_tc``: d <= 66, k <= 24), "simt" runs
+    the CUDA-core kernel (``fd_knn_sqdist``: any d <= 1024, k <= 64), "auto"
+    takes "tc" where it applies.  Both return the same exactly computed
+    squared distances (fp32 coordinate differences)."""
     dev = native.require_device()
     Qd = to_device(Q, torch.float32, dev).contiguous()
     Kd = Qd if K is None else to_device(K, torch.float32, dev).contiguous()
     nq, d = Qd.shape
+    nk = Kd.shape[0]
     out = torch.empty((nq, k), dtype=torch.float32, device=dev)
-    native.check(native.load().fd_knn_sqdist(native._ptr(Qd), nq, native._ptr(Kd), Kd.shape[0], d, k,
-                                             native._ptr(out), native._stream(dev)))
+    lib = native.load()
+    if method not in ("auto", "tc", "simt"):
+        raise ValueError(f"method must be auto, tc or simt (got {method!r})")
+    if method == "tc" or (method == "auto" and d <= 66 and k <= 24 and 1 <= k <= nk and nq > 0):
+        nb = int(lib.fd_knn_tc_workspace_bytes(nq, nk, d, k))
+        ws = torch.empty(nb + 256, dtype=torch.uint8, device=dev)
+        base = ws.data_ptr()
+        aligned = (base + 255) & ~255
+        native.check(lib.fd_knn_sqdist_tc(native._ptr(Qd), nq, native._ptr(Kd), nk, d, k, native._ptr(out),
+                                          native.ctypes.c_void_p(aligned), nb, native._stream(dev)))
+        return out
+    native.check(lib.fd_knn_sqdist(native._ptr(Qd), nq, native._ptr(Kd), nk, d, k,
+                                   native._ptr(out), native._stream(dev)))
     return out
 
 

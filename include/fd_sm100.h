@@ -239,6 +239,19 @@ int fd_comm_destroy(void* comm);
 int fd_knn_sqdist(const float* Q, int64_t nq, const float* K, int64_t nk, int d, int k, float* out,
                   void* stream);
 
+/* Same result as fd_knn_sqdist on the tensor cores: every (query, key) pair is
+ * screened with the fp32-class split operands (tcgen05, the C = k + 8 or more
+ * best keys per row and key split kept), then the candidates' squared
+ * distances are recomputed exactly as fd_knn_sqdist computes them (fp32
+ * coordinate differences) and the k smallest written ascending.  Replaces the
+ * dense sort of knn_bandwidth, FD/utils.py:31-52.  1 <= d <= 66, 1 <= k <= 24,
+ * k <= nk; workspace fd_knn_tc_workspace_bytes(nq, nk, d, k) (packed operands
+ * and candidates).  Synchronises `stream` once (the packing scale comes from
+ * the data's largest centred norm). */
+size_t fd_knn_tc_workspace_bytes(int64_t nq, int64_t nk, int d, int k);
+int fd_knn_sqdist_tc(const float* Q, int64_t nq, const float* K, int64_t nk, int d, int k, float* out,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* out[i][j] = ||x_i - x_j||^2 for a sample of m <= 65535 rows (the median
  * heuristic, median_bandwidth, FD/utils.py:16-28). */
 int fd_pairwise_sqdist(const float* X, int64_t m, int d, float* out, void* stream);

@@ -63,25 +63,30 @@ def _exact_knn(Q, K, k):
     return np.sort(d2, axis=1)[:, :k]
 
 
+@pytest.mark.parametrize("method", ["tc", "simt"])
 @pytest.mark.parametrize("nq,nk,d,k", [(300, 20_000, 64, 16), (257, 5_001, 3, 8), (130, 3_000, 130, 64),
-                                       (64, 1_000, 5, 33), (1, 1, 2, 1)])
-def test_knn_sqdist_vs_exact(nq, nk, d, k):
+                                       (64, 1_000, 5, 33), (1, 1, 2, 1), (1000, 70_000, 66, 24),
+                                       (129, 300, 16, 7)])
+def test_knn_sqdist_vs_exact(nq, nk, d, k, method):
     from flashdiffusion_b200.utils import knn_sqdist
+    if method == "tc" and (d > 66 or k > 24):
+        pytest.skip("tensor-core kNN covers d <= 66, k <= 24")
     rng = np.random.default_rng(nq + nk + d + k)
     K = rng.standard_normal((nk, d)).astype(np.float32)
     Q = K[rng.integers(0, nk, nq)] + 0.05 * rng.standard_normal((nq, d)).astype(np.float32)
-    out = knn_sqdist(Q, K, k).cpu().numpy()
+    out = knn_sqdist(Q, K, k, method=method).cpu().numpy()
     ref = _exact_knn(Q, K, k)
     assert out.shape == (nq, k)
     assert np.all(np.diff(out, axis=1) >= 0)
     np.testing.assert_allclose(out, ref, rtol=2e-6, atol=1e-6 * ref.max())
 
 
-def test_knn_self_is_zero_and_duplicates_count():
+@pytest.mark.parametrize("method", ["tc", "simt"])
+def test_knn_self_is_zero_and_duplicates_count(method):
     from flashdiffusion_b200.utils import knn_sqdist
     X = np.random.default_rng(3).standard_normal((500, 7)).astype(np.float32)
     X = np.concatenate([X, X[:10]])          # 10 exact duplicates
-    out = knn_sqdist(X, None, 3).cpu().numpy()
+    out = knn_sqdist(X, None, 3, method=method).cpu().numpy()
     assert np.all(out[:, 0] == 0)
     assert np.all(out[:10, 1] == 0) and np.all(out[500:, 1] == 0)
 
@@ -104,3 +109,16 @@ def test_knn_bandwidth_at_c2_size_row_subset():
     out = knn_sqdist(X, None, 8).cpu().numpy()[rows]
     ref = np.concatenate([_exact_knn(X[r:r + 1], X, 8) for r in rows])
     np.testing.assert_allclose(out, ref, rtol=2e-6, atol=1e-6 * ref.max())
+
+
+def test_knn_tc_matches_simt_bitwise_at_c2_size_rows():
+    """Both kernels compute the selected squared distances with the same fp32 arithmetic, so on
+    configuration-2 data (200k x 200k, d=64) the tensor-core screen + exact refinement returns
+    exactly the CUDA-core kernel's values on a row subset."""
+    from flashdiffusion_b200 import synthetic
+    from flashdiffusion_b200.utils import knn_sqdist
+    X, _ = synthetic.gaussian_mixture(n=200_000, d=64, seed=1)
+    a = knn_sqdist(X, None, 8, method="tc").cpu().numpy()
+    rows = np.random.default_rng(9).choice(X.shape[0], 2000, replace=False)
+    b = knn_sqdist(X[rows], X, 8, method="simt").cpu().numpy()
+    assert np.array_equal(a[rows], b)
