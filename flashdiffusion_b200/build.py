@@ -60,6 +60,25 @@ def build_cuda(verbose=False, force=False, extra=()):
     return LIB
 
 
+def build_profile(force=False):
+    """libfd_sm100_prof.so: the same library with the block kernel's wait-time
+    counters compiled in (-DFD_PROFILE_WAITS; fd_debug_wait_cycles)."""
+    prof = os.path.join(PKG, "libfd_sm100_prof.so")
+    cu = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    deps = cu + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "fd_sm100.h")]
+    if not force and not _stale(prof, deps):
+        return prof
+    cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+           "--expt-relaxed-constexpr", "-DFD_PROFILE_WAITS", "-I", os.path.join(ROOT, "include"),
+           "-o", prof + ".tmp", *cu, "-ldl"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("nvcc failed building libfd_sm100_prof.so")
+    os.replace(prof + ".tmp", prof)
+    return prof
+
+
 def build_synth(force=False):
     src = os.path.join(CSRC, "synth_host.c")
     if not force and not _stale(SYNTH, [src]):
