@@ -64,6 +64,22 @@ __device__ __forceinline__ void keep_best(float (&v)[C], int (&ix)[C], float x, 
     }
 }
 
+// Screen 32 scores (keys key0 + col0 .. + 31; columns >= valid are past the
+// last key and ignored).
+template <int C>
+__device__ __forceinline__ void screen32(const uint32_t (&v)[32], int col0, int64_t key0, int valid, float (&best)[C],
+                                         int (&bix)[C]) {
+    float m = __uint_as_float(v[0]);
+#pragma unroll
+    for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
+    if (m <= best[C - 1]) return;
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i) {
+        const float x = __uint_as_float(v[i]);
+        if (x > best[C - 1] && col0 + i < valid) keep_best<C>(best, bix, x, (int)(key0 + col0 + i));
+    }
+}
+
 template <int KF, int NW, int C>
 __global__ void __launch_bounds__(NTHREADS, 1)
 knn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
@@ -173,17 +189,24 @@ knn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ C
             ptx::tc_fence_after();
             const int64_t key0 = (jt0 + t) * BN;
             const int valid = (int)(nk - key0 < BN ? nk - key0 : BN);   // keys past nk read zero rows
-            uint32_t v[16];
-#pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
-                ptx::tmem_ld16(t_lane + b * BN + c * 16, v);
-                ptx::tmem_wait_ld16(v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float x = __uint_as_float(v[i]);
-                    if (x > best[C - 1] && c * 16 + i < valid) keep_best<C>(best, bix, x, (int)(key0 + c * 16 + i));
-                }
-            }
+            // four 32-column loads, the next in flight while this one is
+            // screened; a block of 32 scores is looked at one by one only when
+            // its maximum beats the current C-th best (rare after the first
+            // tiles), so the common case is a max-reduction per 32 scores
+            uint32_t va[32], vb[32];
+            const uint32_t tb = t_lane + b * BN;
+            ptx::tmem_ld32(tb, va);
+            ptx::tmem_wait_ld(va);
+            ptx::tmem_ld32(tb + 32, vb);
+            screen32<C>(va, 0, key0, valid, best, bix);
+            ptx::tmem_wait_ld(vb);
+            ptx::tmem_ld32(tb + 64, va);
+            screen32<C>(vb, 32, key0, valid, best, bix);
+            ptx::tmem_wait_ld(va);
+            ptx::tmem_ld32(tb + 96, vb);
+            screen32<C>(va, 64, key0, valid, best, bix);
+            ptx::tmem_wait_ld(vb);
+            screen32<C>(vb, 96, key0, valid, best, bix);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&sempty[b]);
