@@ -65,18 +65,28 @@ __device__ __forceinline__ void keep_best(float (&v)[C], int (&ix)[C], float x, 
 }
 
 // Screen 32 scores (keys key0 + col0 .. + 31; columns >= valid are past the
-// last key and ignored).
+// last key and ignored).  A bit mask of the scores that beat this thread's
+// C-th best is formed with constant register indices; the rare scores that
+// qualify are then fetched again from TMEM one column at a time (a warp-uniform
+// column, the union of the lanes' masks), so no register array is ever
+// indexed dynamically (which would move it to local memory).
 template <int C>
-__device__ __forceinline__ void screen32(const uint32_t (&v)[32], int col0, int64_t key0, int valid, float (&best)[C],
-                                         int (&bix)[C]) {
-    float m = __uint_as_float(v[0]);
+__device__ __forceinline__ void screen32(const uint32_t (&v)[32], uint32_t tcol, int col0, int64_t key0, int valid,
+                                         float (&best)[C], int (&bix)[C]) {
+    const float thr = best[C - 1];
+    uint32_t mask = 0;
 #pragma unroll
-    for (int i = 1; i < 32; ++i) m = fmaxf(m, __uint_as_float(v[i]));
-    if (m <= best[C - 1]) return;
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i) {
-        const float x = __uint_as_float(v[i]);
-        if (x > best[C - 1] && col0 + i < valid) keep_best<C>(best, bix, x, (int)(key0 + col0 + i));
+    for (int i = 0; i < 32; ++i)
+        mask |= (__uint_as_float(v[i]) > thr && col0 + i < valid) ? (1u << i) : 0u;
+    uint32_t any = __reduce_or_sync(0xffffffffu, mask);
+    while (any) {
+        const int i = __ffs(any) - 1;
+        any &= any - 1;
+        uint32_t x;
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(x) : "r"(tcol + (uint32_t)i) : "memory");
+        asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(x) :: "memory");
+        const float xf = __uint_as_float(x);
+        if (((mask >> i) & 1u) && xf > best[C - 1]) keep_best<C>(best, bix, xf, (int)(key0 + col0 + i));
     }
 }
 
@@ -190,23 +200,21 @@ knn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ C
             const int64_t key0 = (jt0 + t) * BN;
             const int valid = (int)(nk - key0 < BN ? nk - key0 : BN);   // keys past nk read zero rows
             // four 32-column loads, the next in flight while this one is
-            // screened; a block of 32 scores is looked at one by one only when
-            // its maximum beats the current C-th best (rare after the first
-            // tiles), so the common case is a max-reduction per 32 scores
+            // screened
             uint32_t va[32], vb[32];
             const uint32_t tb = t_lane + b * BN;
             ptx::tmem_ld32(tb, va);
             ptx::tmem_wait_ld(va);
             ptx::tmem_ld32(tb + 32, vb);
-            screen32<C>(va, 0, key0, valid, best, bix);
+            screen32<C>(va, tb, 0, key0, valid, best, bix);
             ptx::tmem_wait_ld(vb);
             ptx::tmem_ld32(tb + 64, va);
-            screen32<C>(vb, 32, key0, valid, best, bix);
+            screen32<C>(vb, tb + 32, 32, key0, valid, best, bix);
             ptx::tmem_wait_ld(va);
             ptx::tmem_ld32(tb + 96, vb);
-            screen32<C>(va, 64, key0, valid, best, bix);
+            screen32<C>(va, tb + 64, 64, key0, valid, best, bix);
             ptx::tmem_wait_ld(vb);
-            screen32<C>(vb, 96, key0, valid, best, bix);
+            screen32<C>(vb, tb + 96, 96, key0, valid, best, bix);
             ptx::tc_fence_before();
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(&sempty[b]);
