@@ -67,7 +67,7 @@ extern "C" int fd_apply_noalloc(const void* Qop, int64_t nq, const void* Kop, in
         return set_error(FD_ERR_WORKSPACE,
                          "fd_apply_noalloc: nk=%lld, r=%d needs %zu B of scratch (%zu B of it even for one key) but "
                          "the static scratch holds %zu B; limits on a 148-SM GPU: r=1 up to about 1.9 million keys, "
-                         "r=2..16 up to about 44,000 keys, r>=17 not supported; use fd_apply with a workspace",
+                         "r=2..16 up to about 55,000 keys, r>=17 not supported; use fd_apply with a workspace",
                          (long long)nk, r, need, fixed, (size_t)FD_NOALLOC_SCRATCH_BYTES);
     }
     void* scratch = nullptr;

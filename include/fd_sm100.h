@@ -160,7 +160,7 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
  * Limits: 16-bit tiles only (FD_TILE_F16 / FD_TILE_BF16) and
  * fd_apply_workspace_bytes(nq, nk, r, tile) <= FD_NOALLOC_SCRATCH_BYTES, which
  * on a 148-SM B200 means: r = 1 up to about 1.9 million keys; r = 2..16 up to
- * about 44,000 keys (the block path's cross-CTA partial sums take 4.6 MiB
+ * about 55,000 keys (the block path's cross-CTA partial sums take 4.6 MiB
  * whatever nk is); r >= 17 not supported (those partial sums alone exceed the
  * array).  Larger sizes return FD_ERR_WORKSPACE with a message naming nk, r
  * and the bytes needed, before any launch.
@@ -287,12 +287,9 @@ int fd_selftest_wait_timeout(int64_t limit_ns, void* stream);
  * before the sum moves to fp32 registers (1..64; 0 = default: 8 for the 16-bit
  * tiles, 1 for FD_TILE_F16X3).  The tensor-core accumulation rounds toward
  * zero, so fewer tiles per group give a smaller bias (about 7.5e-7 per tile of
- * group) at some speed.  products: 4 (the 16-bit default: P and U both split
- * hi/lo, the small correction product P_lo U_hi on e4m3 operands, 12 instead
- * of 16 tensor-core instructions per 128 keys), 3 (all three products on fp16
- * operands; the fp32-class tiles always use it) or 2 (16-bit tiles only: P
- * rounded once to fp16; faster, 2^-12 noise per kernel value).  0 restores the
- * default.  Not thread-safe against concurrent
+ * group) at some speed.  products: 3 (default, P and U both split hi/lo) or 2
+ * (16-bit tiles only: P rounded once to fp16; faster, 2^-12 noise per kernel
+ * value).  0 restores the default.  Not thread-safe against concurrent
  * launches from other host threads. */
 int fd_set_block_options(int group_tiles, int products);
 
