@@ -89,7 +89,7 @@ def test_argument_errors_before_launch(lib):
     assert lib.fd_rope_windows(fake, 2, 2, fake, 1, 1, 10, 2, 3, 1, 3, 1.0, None, 0, fake, fake, fake, None) == native.FD_ERR_ARG
     # block options and the wait self-test validate their arguments
     assert lib.fd_set_block_options(65, 0) == native.FD_ERR_ARG
-    assert lib.fd_set_block_options(0, 5) == native.FD_ERR_ARG
+    assert lib.fd_set_block_options(0, 4) == native.FD_ERR_ARG
     assert lib.fd_set_block_options(0, 0) == native.FD_OK
     assert lib.fd_selftest_wait_timeout(10, None) == native.FD_ERR_ARG
 
