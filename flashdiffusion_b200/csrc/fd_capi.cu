@@ -49,9 +49,8 @@ static int cols_per_launch(int tile, int r) {
 static size_t rhs_bytes(int64_t nk, int r, int tile) {
     const int rc = std::min(r, cols_per_launch(tile, r));
     const int64_t nk_pad = round_up(std::max<int64_t>(nk, 1), 128);
-    if (is_tc_tile(tile) && r > 1)   // fp16 hi/lo U^T, column words, the e4m3 copy of U_hi^T
-        return align256(sizeof(__half) * 2 * (size_t)nk_pad * block_rp(rc)) + align256(sizeof(float) * 128) +
-               align256((size_t)nk_pad * block_rp(rc));
+    if (is_tc_tile(tile) && r > 1)
+        return align256(sizeof(__half) * 2 * (size_t)nk_pad * block_rp(rc)) + align256(sizeof(float) * 128);
     return align256(sizeof(float) * (size_t)nk_pad * rc);
 }
 
@@ -164,10 +163,8 @@ int fd_apply(const void* Qop, int64_t nq, const void* Kop, int64_t nk, int d, in
             __half* ut = (__half*)ws;
             float* colscale = (float*)(ws + align256(sizeof(__half) * 2 * (size_t)nk_pad * rp));
             unsigned* colmax = (unsigned*)(colscale + 64);
-            uint8_t* ut8 = (uint8_t*)colscale + align256(sizeof(float) * 128);
-            FD_TRY(launch_rhs_f16t(V, v_dtype, nk, nk_pad, r, c0, rc, rp, col_scale, col_h, colmax, ut, colscale,
-                                   block_uses_fp8(tile) ? ut8 : nullptr, s));
-            FD_TRY(launch_tc_block(Qop, nq, Kop, nk, d, tile, ut, ut8, nk_pad, colscale, rc, ep, kws, kws_bytes, s));
+            FD_TRY(launch_rhs_f16t(V, v_dtype, nk, nk_pad, r, c0, rc, rp, col_scale, col_h, colmax, ut, colscale, s));
+            FD_TRY(launch_tc_block(Qop, nq, Kop, nk, d, tile, ut, nk_pad, colscale, rc, ep, kws, kws_bytes, s));
             continue;
         }
         FD_TRY(launch_rhs_f32(V, v_dtype, nk, nk_pad, r, c0, rc, col_scale, col_h, u, s));

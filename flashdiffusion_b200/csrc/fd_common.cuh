@@ -4,7 +4,6 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
-#include <cuda_fp8.h>
 #include <stdint.h>
 
 #include "../../include/fd_sm100.h"

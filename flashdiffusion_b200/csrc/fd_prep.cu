@@ -229,15 +229,11 @@ __global__ void rhs_colmax_kernel(const void* __restrict__ V, int v_dtype, int64
 // Transposed fp16 hi/lo right-hand side with a power-of-two scale per column:
 // with x = u_jc / 2^k_c, ut[c*ld + j] = fp16(x) and ut[(rp + c)*ld + j] =
 // fp16(x - fp16(x)); colscale[c] = 2^k_c with max_j |u_jc| / 2^k_c in [1/2, 1).
-// Rows rc..rp-1 (of both halves) and columns nk..ld-1 are zero.  If ut8 is not
-// null, ut8[c*ld + j] = e4m3(256 fp16(x)): the 8-bit copy of the hi part that
-// the block kernel's correction product P_lo U_hi reads (|256 x| < 256 fits
-// e4m3's range of 448; its 3-bit mantissa is enough for a term 2^-12 the size
-// of the product).
+// Rows rc..rp-1 (of both halves) and columns nk..ld-1 are zero.
 __global__ void rhs_f16t_kernel(const void* __restrict__ V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0,
                                 int rc, int rp, const float* __restrict__ cs, const float* __restrict__ ch,
                                 const unsigned* __restrict__ colmax, __half* __restrict__ ut,
-                                float* __restrict__ colscale, uint8_t* __restrict__ ut8) {
+                                float* __restrict__ colscale) {
     if (blockIdx.x == 0)
         for (int c = threadIdx.x; c < rp; c += blockDim.x) {
             int k = 0;
@@ -263,7 +259,6 @@ __global__ void rhs_f16t_kernel(const void* __restrict__ V, int v_dtype, int64_t
         const __half hi = __float2half_rn(val);
         ut[e] = hi;
         ut[e + ld * rp] = __float2half_rn(val - __half2float(hi));
-        if (ut8) ut8[e] = (uint8_t)__nv_cvt_float_to_fp8(256.0f * __half2float(hi), __NV_SATFINITE, __NV_E4M3);
     }
 }
 
@@ -359,8 +354,7 @@ int launch_rhs_bf16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv
 }
 
 int launch_rhs_f16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0, int rc, int rp,
-                    const float* cs, const float* ch, unsigned* colmax, __half* ut, float* colscale, uint8_t* ut8,
-                    cudaStream_t s) {
+                    const float* cs, const float* ch, unsigned* colmax, __half* ut, float* colscale, cudaStream_t s) {
     FD_CUDA_TRY(cudaMemsetAsync(colmax, 0, sizeof(unsigned) * rp, s));
     if (nk > 0) {
         const int g1 = (int)std::min<int64_t>(cdiv(nk * rc, 256), 148 * 4);
@@ -368,7 +362,7 @@ int launch_rhs_f16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv,
         FD_CUDA_TRY(cudaGetLastError());
     }
     const int g2 = (int)std::min<int64_t>(cdiv(ld * rp, 256), 148 * 16);
-    rhs_f16t_kernel<<<g2, 256, 0, s>>>(V, v_dtype, nk, ld, ldv, c0, rc, rp, cs, ch, colmax, ut, colscale, ut8);
+    rhs_f16t_kernel<<<g2, 256, 0, s>>>(V, v_dtype, nk, ld, ldv, c0, rc, rp, cs, ch, colmax, ut, colscale);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }

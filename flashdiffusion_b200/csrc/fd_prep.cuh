@@ -14,8 +14,7 @@ int launch_rhs_f32(const void* V, int v_dtype, int64_t nk, int64_t nk_pad, int l
 int launch_rhs_bf16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0, int rc,
                      const float* cs, const float* ch, __nv_bfloat16* ut, cudaStream_t s);
 int launch_rhs_f16t(const void* V, int v_dtype, int64_t nk, int64_t ld, int ldv, int c0, int rc, int rp,
-                    const float* cs, const float* ch, unsigned* colmax, __half* ut, float* colscale, uint8_t* ut8,
-                    cudaStream_t s);
+                    const float* cs, const float* ch, unsigned* colmax, __half* ut, float* colscale, cudaStream_t s);
 int launch_dmap_weights(const float* D, int64_t n, float alpha, float* w, cudaStream_t s);
 int launch_dmap_rscale(const float* Kw, const float* w, int64_t n, float* Da, float* rs, cudaStream_t s);
 
@@ -54,13 +53,11 @@ int launch_tc(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, i
 
 // 16-bit tcgen05 tiles with a block right-hand side (up to 64 columns per launch).
 int block_rp(int rc);
-// The block kernel's correction product P_lo U_hi runs on 8-bit operands for this tile
-bool block_uses_fp8(int tile);
 int block_max_cols(int d);
 size_t tc_block_workspace_bytes(int rp);
 int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile, const void* ut,
-                    const void* ut8, int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws,
-                    size_t ws_bytes, cudaStream_t s);
+                    int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes,
+                    cudaStream_t s);
 
 int read_and_clear_status(cudaStream_t s, int* status);
 // Device address of the library's status word (bounded-wait timeouts, fp16 range).

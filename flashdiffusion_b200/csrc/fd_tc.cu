@@ -661,21 +661,6 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols,
     return FD_OK;
 }
 
-int make_u8_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
-    EncodeTiledFn enc;
-    FD_TRY(get_encode(&enc));
-    FD_CHECK_ARG(((uintptr_t)ptr & 15) == 0 && cols % 16 == 0, "8-bit operand alignment");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols};
-    cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(FD_ERR_CUDA, "cuTensorMapEncodeTiled (8-bit) failed (%d)", (int)r);
-    return FD_OK;
-}
-
 void split_kd(int kd, int* kf, int* nw) {
     *kf = kd / 64;
     *nw = kd % 64;

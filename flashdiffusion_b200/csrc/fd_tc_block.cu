@@ -97,16 +97,13 @@ struct Cfg {
     // its own) and one issuer consumes them in order.
     static constexpr bool WIDE = KF * 64 + NW > 208;
     static constexpr uint32_t STAGE_BYTES = WIDE ? KBOX_BYTES : G::bytes(BN);
-    static constexpr uint32_t UT8_BOX = RP * 128;               // RP rows x 128 keys of e4m3 U_hi^T
-    static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX + UT8_BOX;
+    static constexpr uint32_t USTAGE_BYTES = 4 * UT_BOX;
     static constexpr uint32_t BUDGET = 222u * 1024u - Q_BYTES;
     static constexpr uint32_t ACC_BYTES = RP * BM * 4;     // running O sums of the segment
     // U^T tiles live from their load to their P.U: 4 stages unless that leaves
-    // fewer than 3 K stages, 3 unless that leaves fewer than 2 (2 for the wide
-    // operands)
+    // fewer than 3 K stages (2 for the wide operands)
     static constexpr int USTAGES =
-        WIDE ? 2 : ((BUDGET - ACC_BYTES - 4 * USTAGE_BYTES) / STAGE_BYTES >= 3
-                        ? 4 : ((BUDGET - ACC_BYTES - 3 * USTAGE_BYTES) / STAGE_BYTES >= 2 ? 3 : 2));
+        WIDE ? 2 : ((BUDGET - ACC_BYTES - 4 * USTAGE_BYTES) / STAGE_BYTES >= 3 ? 4 : 3);
     static constexpr int K_RAW = (int)((BUDGET - ACC_BYTES - USTAGES * USTAGE_BYTES) / STAGE_BYTES);
     static constexpr int STAGES = K_RAW > (WIDE ? 8 : 6) ? (WIDE ? 8 : 6) : (K_RAW < 2 ? 2 : K_RAW);
     static_assert(!WIDE || STAGES >= 3, "wide operands need at least 3 box slots");
@@ -179,29 +176,6 @@ __device__ __forceinline__ void exp2_to_f16x2(const uint32_t (&v)[16], uint32_t 
     }
 }
 
-// 16 S values -> P = 2^S as fp16 hi parts (8 registers, key 2c in the low
-// half) and the remainders P - hi scaled by 2^20 as e4m3 (4 registers, four
-// keys each, lowest key in the lowest byte) into lo8[off .. off + 4).  |P - hi|
-// <= 2^-12 P <= 2^-12, so the scaled remainder stays inside e4m3's range.
-template <int N>
-__device__ __forceinline__ void exp2_to_f16_lo8(const uint32_t (&v)[16], uint32_t (&hi)[8], uint32_t (&lo8)[N], int off) {
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        uint32_t q[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const float e0 = ptx::ex2_mufu(__uint_as_float(v[2 * (i + u)]));
-            const float e1 = ptx::ex2_mufu(__uint_as_float(v[2 * (i + u) + 1]));
-            const __half2 h = __floats2half2_rn(e0, e1);
-            const float2 hf = __half22float2(h);
-            hi[i + u] = *reinterpret_cast<const uint32_t*>(&h);
-            const float2 r = make_float2((e0 - hf.x) * 0x1p20f, (e1 - hf.y) * 0x1p20f);
-            q[u] = (uint32_t)__nv_cvt_float2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
-        }
-        lo8[off + i / 2] = q[0] | (q[1] << 16);
-    }
-}
-
 // 16 S values -> P = 2^S rounded once to fp16, 8 registers, key 2c in the low half.
 __device__ __forceinline__ void exp2_to_f16(const uint32_t (&v)[16], uint32_t (&p)[8]) {
 #pragma unroll
@@ -216,11 +190,9 @@ template <int KF, int NW, int RP>
 __global__ void __launch_bounds__(NTHREADS, 1)
 tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                 const __grid_constant__ CUtensorMap tmq_n, const __grid_constant__ CUtensorMap tmk_n,
-                const __grid_constant__ CUtensorMap tmu, const __grid_constant__ CUtensorMap tmu8,
-                const float* __restrict__ colscale, int rc,
+                const __grid_constant__ CUtensorMap tmu, const float* __restrict__ colscale, int rc,
                 int64_t nq, uint32_t idesc_qk, uint32_t idesc_pv, Sched sc, RowEpilogue ep,
-                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2, int ogroup, int three,
-                int fp8) {
+                double* __restrict__ part, int* __restrict__ status, uint32_t idesc_pv2, int ogroup, int three) {
     using C = Cfg<KF, NW, RP>;
     using G = typename C::G;
     extern __shared__ uint8_t smem_raw[];
@@ -344,12 +316,11 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 // U_hi^T rows [0, RP), U_lo^T rows [RP, 2 RP) of the same map
                 if (!FD_WAIT(2, &uempty[ustage], uph ^ 1, abort, status, WAIT_LIMIT_NS)) break;
                 uint8_t* su = sU + ustage * C::USTAGE_BYTES;
-                ptx::mbar_expect_tx(&ufull[ustage], fp8 ? C::USTAGE_BYTES : 4 * C::UT_BOX);
+                ptx::mbar_expect_tx(&ufull[ustage], C::USTAGE_BYTES);
                 for (int part2 = 0; part2 < 2; ++part2)
                     for (int h = 0; h < 2; ++h)
                         ptx::tma_load_2d(su + (h * 2 + part2) * C::UT_BOX, &tmu, &ufull[ustage],
                                          (int)(jt * BN + h * 64), part2 * RP);
-                if (fp8) ptx::tma_load_2d(su + 4 * C::UT_BOX, &tmu8, &ufull[ustage], (int)(jt * BN), 0);
                 if (++ustage == C::USTAGES) { ustage = 0; uph ^= 1; }
             }
         }
@@ -445,15 +416,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 ptx::tc_fence_after();
                 const uint32_t ut = u_base + ustage * C::USTAGE_BYTES;
                 FD_SPAN_BEGIN;
-                if (fp8 && t == 1) {
-                    // the correction P_lo U_hi on 8-bit operands: 32 keys per
-                    // instruction, P_lo (e4m3, 8 columns) after each pair's P_hi
-                    for (int j = 0; j < BN / 32; ++j)
-                        ptx::umma_ts_f8(dcol, tmem + pb * BN + 32 * j + 8,
-                                        ptx::sw128_kmajor_desc(ut + 4 * C::UT_BOX + 32 * j), idesc,
-                                        (fresh && j == 0) ? 0u : 1u);
-                }
-                for (int ks = ks0; ks < ks1 && !(fp8 && t == 1); ++ks) {
+                for (int ks = ks0; ks < ks1; ++ks) {
                     // U_hi^T rows then U_lo^T rows of this 64-key box: one 2 RP-row operand
                     const uint32_t off = (ks >> 2) * 2 * C::UT_BOX + (ks & 3) * 32;
                     // keys 16ks..16ks+15: P (or P_hi) in 8 columns, P_lo in the next 8
@@ -508,24 +471,7 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 uint32_t va[16], vb[16], ph[8], pl[8];
                 ptx::tmem_ld16(tb, va);
                 ptx::tmem_wait_ld16(va);
-                if (three && fp8) {
-                    // P_hi (fp16) of each 16 keys over their first 8 S columns;
-                    // P_lo (e4m3, scaled by 2^20) of each 32 keys over the last 8
-                    // S columns of the first 16 of them
-                    uint32_t l8[8];
-#pragma unroll 1
-                    for (int c = 0; c < BN / 16; c += 2) {
-                        ptx::tmem_ld16(tb + (c + 1) * 16, vb);
-                        exp2_to_f16_lo8(va, ph, l8, 0);
-                        tmem_st8(tb + c * 16, ph);
-                        ptx::tmem_wait_ld16(vb);
-                        if (c + 2 < BN / 16) ptx::tmem_ld16(tb + (c + 2) * 16, va);
-                        exp2_to_f16_lo8(vb, ph, l8, 4);
-                        tmem_st8(tb + (c + 1) * 16, ph);
-                        tmem_st8(tb + c * 16 + 8, l8);
-                        if (c + 2 < BN / 16) ptx::tmem_wait_ld16(va);
-                    }
-                } else if (three) {
+                if (three) {
 #pragma unroll 1
                     for (int c = 0; c < BN / 16; c += 2) {
                         ptx::tmem_ld16(tb + (c + 1) * 16, vb);
@@ -573,9 +519,8 @@ tc_block_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     float o[16], t[16];
                     tmem_ld_cols<16>(t_lane + O_COL + c16, o);
                     tmem_ld_cols<16>(t_lane + O_COL + 2 * RP + c16, t);
-                    const float s2 = fp8 ? 0x1p-28f : 1.0f;   // undo the 2^20 (P_lo) x 2^8 (U_hi) of the 8-bit product
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = fmaf(t[i], s2, o[i]);
+                    for (int i = 0; i < 16; ++i) o[i] += t[i];
                     tmem_ld_cols<16>(t_lane + O_COL + RP + c16, t);
                     if (!three) {
                         float t4[16];
@@ -646,7 +591,7 @@ size_t tc_block_workspace_bytes(int rp) {
 }
 
 struct BlockArgs {
-    CUtensorMap mq, mk, mqn, mkn, mu, mu8;
+    CUtensorMap mq, mk, mqn, mkn, mu;
     const float* colscale;
     int rc;
     int64_t nq;
@@ -656,7 +601,6 @@ struct BlockArgs {
     double* part;
     int ogroup;
     int three;
-    int fp8;
 };
 
 template <int KF, int NW, int RP>
@@ -667,8 +611,8 @@ static int launch_block_t(const BlockArgs& a, cudaStream_t s) {
     FD_CUDA_TRY(cudaFuncSetAttribute(tcb::tc_block_kernel<KF, NW, RP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)C::SMEM_ALLOC));
     tcb::tc_block_kernel<KF, NW, RP><<<a.sc.grid, tcb::NTHREADS, C::SMEM_ALLOC, s>>>(
-        a.mq, a.mk, a.mqn, a.mkn, a.mu, a.mu8, a.colscale, a.rc, a.nq, a.iqk, a.ipv, a.sc, a.ep, a.part, status,
-        ptx::idesc_f32acc(tcb::BM, 2 * RP, true), a.ogroup, a.three, a.fp8);
+        a.mq, a.mk, a.mqn, a.mkn, a.mu, a.colscale, a.rc, a.nq, a.iqk, a.ipv, a.sc, a.ep, a.part, status,
+        ptx::idesc_f32acc(tcb::BM, 2 * RP, true), a.ogroup, a.three);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
 }
@@ -688,19 +632,13 @@ static int block_ogroup(int tile) {
     return tile == FD_TILE_F16X3 ? 1 : 8;
 }
 
-// Products per P.U, as fd_set_block_options names them:
-//   3  P_hi U_hi + P_hi U_lo + P_lo U_hi, all fp16 operands (P and U both to
-//      ~22 bits): the fp32-class tiles always, the 16-bit tiles on request;
-//   4  the same with the correction P_lo U_hi on e4m3 operands (32 keys per
-//      instruction instead of 16: 12 P.U instructions per 128 keys instead of
-//      16; the correction is 2^-12 the size of the product, so its 3-bit
-//      mantissas add ~2^-16 relative noise): the 16-bit default;
-//   2  P rounded once to fp16 (P U_hi + P U_lo, 8 instructions): about 2^-12
-//      relative noise per kernel value, which a column whose sum cancels
-//      heavily amplifies past 2e-3.
+// Products per P.U: 3 (P_hi U_hi + P_hi U_lo + P_lo U_hi: P and U both to
+// ~22 bits) by default.  2 rounds P once to fp16 for the 16-bit tiles
+// (P U_hi + P U_lo, half the P.U instructions): about 2^-12 relative noise per
+// kernel value, which a column whose sum cancels heavily can amplify past 2e-3.
 static int block_products(int tile) {
     if (tile == FD_TILE_F16X3) return 3;
-    return g_block_products == 0 ? 4 : g_block_products;
+    return g_block_products == 2 ? 2 : 3;
 }
 
 template <int KF, int NW>
@@ -710,11 +648,9 @@ static int launch_block_kb(int rp, const BlockArgs& a, cudaStream_t s) {
 
 // ut: [2 rp][ld] fp16 transposed, column-scaled right-hand side (hi rows, then
 // lo rows); colscale: rp floats.
-bool block_uses_fp8(int tile) { return block_products(tile) == 4; }
-
 int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, int d, int tile, const void* ut,
-                    const void* ut8, int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws,
-                    size_t ws_bytes, cudaStream_t s) {
+                    int64_t ld, const float* colscale, int rc, const RowEpilogue& ep, void* ws, size_t ws_bytes,
+                    cudaStream_t s) {
     if (nq == 0) return FD_OK;
     if (nk == 0) return launch_zero_rows(nq, rc, ep, s);
     FD_CHECK_ARG(rc >= 1 && rc <= 32, "block tile path: %d columns per launch (max 32)", rc);
@@ -737,9 +673,6 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
         FD_TRY(make_tile_map(&a.mkn, kop, nk, kd, tcb::BN, f16, nw));
     }
     FD_TRY(make_tile_map(&a.mu, ut, 2 * rp, ld, rp, true));   // U_hi^T rows then U_lo^T rows
-    a.fp8 = block_products(tile) == 4;
-    a.mu8 = a.mu;
-    if (a.fp8) FD_TRY(make_u8_map(&a.mu8, ut8, rp, ld, rp));
     a.iqk = ptx::idesc_f32acc(tcb::BM, tcb::BN, f16);
     a.ipv = ptx::idesc_f32acc(tcb::BM, rp, true);
     a.sc = tc::Sched::make(cdiv(nq, tcb::BM), cdiv(nk, tcb::BN), num_sms(), (size_t)nk * kd * 2);
@@ -754,7 +687,7 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
     a.nq = nq;
     a.ep = ep;
     a.ogroup = block_ogroup(tile);
-    a.three = block_products(tile) >= 3;
+    a.three = block_products(tile) == 3;
     switch (kf * 100 + nw) {
         case 16: FD_TRY((launch_block_kb<0, 16>(rp, a, s))); break;
         case 32: FD_TRY((launch_block_kb<0, 32>(rp, a, s))); break;
@@ -788,8 +721,8 @@ int launch_tc_block(const void* qop, int64_t nq, const void* kop, int64_t nk, in
 extern "C" int fd_set_block_options(int group_tiles, int products) {
     if (group_tiles < 0 || group_tiles > 64)
         return fd::set_error(FD_ERR_ARG, "fd_set_block_options: group_tiles %d (0..64)", group_tiles);
-    if (products != 0 && products != 2 && products != 3 && products != 4)
-        return fd::set_error(FD_ERR_ARG, "fd_set_block_options: products %d (0, 2, 3 or 4)", products);
+    if (products != 0 && products != 2 && products != 3)
+        return fd::set_error(FD_ERR_ARG, "fd_set_block_options: products %d (0, 2 or 3)", products);
     fd::g_block_group = group_tiles;
     fd::g_block_products = products;
     return FD_OK;

@@ -223,8 +223,6 @@ __device__ __forceinline__ uint64_t exp2_poly2(uint32_t a, uint32_t b) {
 // with the swizzle that matches box_cols (64 -> 128 B, 32 -> 64 B, 16 -> 32 B).
 int make_tile_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows, bool f16,
                   int box_cols = 64);
-// 2-D map over a [rows][cols] 8-bit row-major matrix, 128 x box_rows boxes, 128-byte swizzle.
-int make_u8_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_rows);
 // kd = 64 kf + nw with nw in {0, 16, 32} (a remainder of 48 takes a full box).
 void split_kd(int kd, int* kf, int* nw);
 int num_sms();
