@@ -401,8 +401,10 @@ def run_ours(args):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         lo = op if emode == "dmap" else ShardedOperator(Qd, Kd, beta, 0.5, "f16", mode=emode, h=hd).fit()
+        # a Krylov basis of 4k vectors (the reference's ARPACK default is 2k+1):
+        # fewer restarts, 224 instead of 237 products at c2 (2.86 s against 3.14-3.42 s)
         vals, _, info = ramp_eigsh(lo, lambda: ShardedOperator(Qd, Kd, beta, 0.5, "f16x3", mode=emode, h=hd).fit(),
-                                   nq, kk, tol=1e-7)
+                                   nq, kk, tol=1e-7, ncv=min(4 * kk, nq))
         torch.cuda.synchronize()
         lt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
         if world > 1:
@@ -413,7 +415,7 @@ def run_ours(args):
         # the Lanczos vector operations alone: one full reorthogonalisation
         # step (fd_lanczos_reorth) against a basis of ncv rows, HBM bytes =
         # three reads of the basis + the vectors, over CUDA-event time
-        ncv = min(max(2 * kk + 1, 20), nq)
+        ncv = min(4 * kk, nq)
         Vb = torch.randn((ncv + 1, nq), dtype=torch.float64, device=dev)
         wv = torch.randn(nq, dtype=torch.float64, device=dev)
         cf = torch.zeros(ncv + 2, dtype=torch.float64, device=dev)
