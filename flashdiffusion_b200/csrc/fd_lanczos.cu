@@ -29,7 +29,12 @@ namespace lz {
 constexpr int CHUNK = 256;     // entries of n per block (one per thread)
 constexpr int THREADS = CHUNK;
 constexpr int WARPS = THREADS / 32;
-constexpr int MAX_ROWS = 96;   // basis rows a step orthogonalises against (96 x 256 x 8 B = 192 KB of V)
+// pass B keeps its chunk of every basis row in shared memory: 128 entries per
+// block (96 rows x 128 x 8 B = 96 KB at most) so that two or three blocks share
+// an SM; passes A and C, which need no such copy, take 256
+constexpr int CHUNK_B = 128;
+constexpr int WARPS_B = CHUNK_B / 32;
+constexpr int MAX_ROWS = 96;   // basis rows a step orthogonalises against
 
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
@@ -78,30 +83,30 @@ __global__ void __launch_bounds__(THREADS) reduce_kernel(const double* __restric
 }
 
 // pass B: w1 = w - V^T h1 (written to w); part = V w1, and ||w1||^2 in row `rows`
-__global__ void __launch_bounds__(THREADS) pass_b_kernel(const double* __restrict__ V, int64_t ldv, int rows,
+__global__ void __launch_bounds__(CHUNK_B) pass_b_kernel(const double* __restrict__ V, int64_t ldv, int rows,
                                                          int64_t n, double* __restrict__ w,
                                                          const double* __restrict__ h1, double* __restrict__ part) {
     extern __shared__ double smem[];
-    double* sV = smem;                       // [rows][CHUNK]
-    double* sw = sV + (size_t)rows * CHUNK;  // [CHUNK]
-    double* sh = sw + CHUNK;                 // [rows]
-    const int64_t base = (int64_t)blockIdx.x * CHUNK;
-    const int cnt = chunk_count(n, base);
+    double* sV = smem;                         // [rows][CHUNK_B]
+    double* sw = sV + (size_t)rows * CHUNK_B;  // [CHUNK_B]
+    double* sh = sw + CHUNK_B;                 // [rows]
+    const int64_t base = (int64_t)blockIdx.x * CHUNK_B;
+    const int cnt = (int)(n - base < CHUNK_B ? n - base : CHUNK_B);
     const int t = threadIdx.x;
-    for (int i = t; i < rows; i += THREADS) sh[i] = h1[i];
-    for (int i = 0; i < rows; ++i) sV[i * CHUNK + t] = t < cnt ? V[(int64_t)i * ldv + base + t] : 0.0;
+    for (int i = t; i < rows; i += CHUNK_B) sh[i] = h1[i];
+    for (int i = 0; i < rows; ++i) sV[i * CHUNK_B + t] = t < cnt ? V[(int64_t)i * ldv + base + t] : 0.0;
     __syncthreads();
     double x = t < cnt ? w[base + t] : 0.0;
-    for (int i = 0; i < rows; ++i) x -= sV[i * CHUNK + t] * sh[i];
+    for (int i = 0; i < rows; ++i) x -= sV[i * CHUNK_B + t] * sh[i];
     sw[t] = x;
     if (t < cnt) w[base + t] = x;
     __syncthreads();
     const int warp = t >> 5, lane = t & 31;
-    for (int i = warp; i <= rows; i += WARPS) {
+    for (int i = warp; i <= rows; i += WARPS_B) {
         double acc = 0.0;
         for (int e = lane; e < cnt; e += 32) {
             const double xe = sw[e];
-            acc += (i < rows ? sV[i * CHUNK + e] : xe) * xe;
+            acc += (i < rows ? sV[i * CHUNK_B + e] : xe) * xe;
         }
         acc = warp_sum(acc);
         if (lane == 0) part[(int64_t)i * gridDim.x + blockIdx.x] = acc;
@@ -146,7 +151,7 @@ using namespace fd;
 
 extern "C" size_t fd_lanczos_workspace_bytes(int64_t n, int rows) {
     if (n < 1 || rows < 0) return 0;
-    const int64_t nblk = cdiv(n, lz::CHUNK);
+    const int64_t nblk = cdiv(n, lz::CHUNK_B);   // the larger partial count (pass B)
     return align256(sizeof(double) * (size_t)nblk * (rows + 1)) + align256(sizeof(double) * (rows + 1));
 }
 
@@ -163,14 +168,15 @@ extern "C" int fd_lanczos_reorth(const double* V, int64_t ldv, int rows, int64_t
                          need);
     FD_CHECK_ARG(workspace && ((uintptr_t)workspace & 255) == 0, "workspace must be non-null and 256-byte aligned");
     const int nblk = (int)cdiv(n, lz::CHUNK);
+    const int nblk_b = (int)cdiv(n, lz::CHUNK_B);
     double* part = (double*)workspace;
-    double* h2s = (double*)((uint8_t*)workspace + align256(sizeof(double) * (size_t)nblk * (rows + 1)));
-    const size_t smem_b = sizeof(double) * ((size_t)rows * lz::CHUNK + lz::CHUNK + rows);
+    double* h2s = (double*)((uint8_t*)workspace + align256(sizeof(double) * (size_t)nblk_b * (rows + 1)));
+    const size_t smem_b = sizeof(double) * ((size_t)rows * lz::CHUNK_B + lz::CHUNK_B + rows);
     FD_CUDA_TRY(cudaFuncSetAttribute(lz::pass_b_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b));
     lz::pass_a_kernel<<<nblk, lz::THREADS, 0, s>>>(V, ldv, rows, n, w, part);
     lz::reduce_kernel<<<rows, lz::THREADS, 0, s>>>(part, nblk, coef);
-    lz::pass_b_kernel<<<nblk, lz::THREADS, smem_b, s>>>(V, ldv, rows, n, w, coef, part);
-    lz::reduce_kernel<<<rows + 1, lz::THREADS, 0, s>>>(part, nblk, h2s);
+    lz::pass_b_kernel<<<nblk_b, lz::CHUNK_B, smem_b, s>>>(V, ldv, rows, n, w, coef, part);
+    lz::reduce_kernel<<<rows + 1, lz::THREADS, 0, s>>>(part, nblk_b, h2s);
     lz::pass_c_kernel<<<nblk, lz::THREADS, 0, s>>>(V, ldv, rows, n, w, h2s, out, coef);
     FD_CUDA_TRY(cudaGetLastError());
     return FD_OK;
